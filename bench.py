@@ -1,0 +1,404 @@
+#!/usr/bin/env python3
+"""Benchmark of the Whisper-encoder hot path on B200: large-v3 encoder forward,
+ctx 1500, clips sharded across GPUs (one encoder replica per GPU, no
+collective on the data path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
+
+A step is one encoder forward over the rank's B clips (default 64, the
+BASELINE batch-64 config; weak scaling: each GPU encodes B clips per step).
+Prints ONE JSON line on rank 0. Synthetic data: random N(0, 0.02) weights of
+the large-v3 architecture, log-mel ~ U[-0.8, 1.2] seeded per clip (no
+checkpoint or audio can be fetched here).
+
+--impl reference times the reference's own CPU implementation of the path --
+its numpy encoder (src/npu_whisper_encoder.py:encoder with np_matmul),
+restated in oracle/encoder_ref.py because the reference's Python cannot travel
+to the GPU box -- on the host cores, one clip per step over a bounded number
+of layers, extrapolated to the 32-layer clip.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "whisper-xdna_b200"))
+
+METRIC = "large-v3 encoder clips/s @ctx1500"
+UNIT = "clips/s"
+N_MELS, D, N_HEAD, N_LAYER, FFN, CTX = 128, 1280, 20, 32, 5120, 1500
+FLOP_PER_CLIP = (N_LAYER * (8 * CTX * D * D + 4 * CTX * D * FFN + 4 * CTX * CTX * D)
+                 + 2 * (2 * CTX) * (3 * N_MELS) * D + 2 * CTX * (3 * D) * D)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=64, help="clips per GPU per step")
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-layers", type=int, default=2,
+                    help="layers in the bounded CPU sample")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ CPU side
+
+def cpu_sample(n_layers, seed=1):
+    """Time the oracle port of the reference's numpy encoder on one clip:
+    frontend, n_layers blocks, ln_post; extrapolate to 32 layers.
+    Returns (clips_per_s, seconds_spent, description)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import encoder_ref as R
+    W = R.make_weights("large-v3", seed=seed, n_layer=n_layers)
+    mel = R.make_mel(N_MELS, 2 * CTX, seed=0)
+    t0 = time.perf_counter()
+    R.encoder_np(W, mel, n_layer=0, n_head=N_HEAD)          # frontend + ln_post
+    t1 = time.perf_counter()
+    R.encoder_np(W, mel, n_layer=n_layers, n_head=N_HEAD)
+    t2 = time.perf_counter()
+    front = t1 - t0
+    per_layer = ((t2 - t1) - front) / n_layers
+    clip_s = front + N_LAYER * per_layer
+    desc = (f"1 clip of large-v3 ctx 1500: frontend+ln_post ({front:.2f} s) and "
+            f"{n_layers} layers ({per_layer:.2f} s/layer) timed, extrapolated to "
+            f"32 layers = {clip_s:.1f} s/clip")
+    return 1.0 / clip_s, t2 - t0, desc
+
+
+def cpu_cores():
+    try:
+        import numpy as np  # noqa: F401
+        from threadpoolctl import threadpool_info
+        n = max((i.get("num_threads", 0) for i in threadpool_info()), default=0)
+        if n:
+            return n
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_sample(1)
+    vals, spent, desc = [], 0.0, ""
+    for _ in range(args.steps):
+        v, s, desc = cpu_sample(args.cpu_layers)
+        vals.append(v)
+        spent += s
+    value = statistics.median(vals)
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "large-v3 encoder forward, ctx 1500, one clip per step "
+                               "(bounded sample)", "model": "large-v3 (random weights)",
+                   "global_batch": 1, "seq_len": CTX, "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+# ------------------------------------------------------------------ GPU side
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_weights_fast(seed):
+    """Random N(0, 0.02) large-v3 weights (torch CPU generator, bf16-exact),
+    LayerNorm 1 / 0, sinusoidal positions, in the reference's W-dict layout."""
+    import numpy as np
+    import torch
+
+    def sinusoids(length, channels, max_timescale=10000):
+        inc = np.log(max_timescale) / (channels // 2 - 1)
+        t = np.arange(length)[:, None] * np.exp(-inc * np.arange(channels // 2))[None, :]
+        return np.concatenate([np.sin(t), np.cos(t)], axis=1).astype(np.float32)
+
+    g = torch.Generator().manual_seed(seed)
+    rn = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    W = {"w.conv1.weight": rn(D, N_MELS, 3), "w.conv1.bias": rn(D),
+         "w.conv2.weight": rn(D, D, 3), "w.conv2.bias": rn(D),
+         "w.positional_embedding": sinusoids(CTX, D),
+         "w.ln_post.weight": np.ones(D, np.float32), "w.ln_post.bias": np.zeros(D, np.float32)}
+    for l in range(N_LAYER):
+        p = f"w.blocks.{l}."
+        W[p + "attn_ln.weight"] = np.ones(D, np.float32)
+        W[p + "attn_ln.bias"] = np.zeros(D, np.float32)
+        W[p + "mlp_ln.weight"] = np.ones(D, np.float32)
+        W[p + "mlp_ln.bias"] = np.zeros(D, np.float32)
+        for n, s in (("attn.query.weight", (D, D)), ("attn.query.bias", (D,)),
+                     ("attn.key.weight", (D, D)), ("attn.value.weight", (D, D)),
+                     ("attn.value.bias", (D,)), ("attn.out.weight", (D, D)),
+                     ("attn.out.bias", (D,)), ("mlp.0.weight", (FFN, D)), ("mlp.0.bias", (FFN,)),
+                     ("mlp.2.weight", (D, FFN)), ("mlp.2.bias", (D,))):
+            W[p + n] = rn(*s)
+    return W
+
+
+def kernel_rooflines(batch, peaks):
+    """Time the encoder's kernels one at a time with CUDA events on the
+    launching stream (inputs larger than L2), on this rank's shapes."""
+    import torch
+    from wxb200 import _lib as L
+    from wxb200 import ops
+    M = batch * CTX
+    dev = "cuda"
+    st = torch.cuda.current_stream()
+    g = torch.Generator(device=dev).manual_seed(7)
+    h = (torch.randn(M, D, device=dev, generator=g)).to(torch.bfloat16)
+    f = (torch.randn(M, FFN, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    qkv = torch.randn(M, 3 * D, device=dev, generator=g).to(torch.bfloat16)
+    x = torch.randn(M, D, device=dev, generator=g)
+    w1 = (torch.randn(FFN, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(D, FFN, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    wqkv = (torch.randn(3 * D, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    b1 = torch.zeros(FFN, device=dev)
+    b2 = torch.zeros(D, device=dev)
+    bq = torch.zeros(3 * D, device=dev)
+    o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+    hb = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+    ones = torch.ones(D, device=dev)
+    zeros = torch.zeros(D, device=dev)
+
+    def timed(fn, reps=10, warm=3):
+        for _ in range(warm):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(reps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps / 1e3
+
+    res = {}
+    fl = 2.0 * M * D * FFN
+    t = timed(lambda: ops.gemm(h, w1, bias=b1, out=f, epilogue=L.WX_EPI_BF16_GELU))
+    res["gemm_fc1_gelu"] = {"s": t, "tflops": fl / t / 1e12}
+    t = timed(lambda: ops.gemm(f, w2, bias=b2, residual=x, out=x, epilogue=L.WX_EPI_F32_RESID))
+    res["gemm_fc2_resid"] = {"s": t, "tflops": fl / t / 1e12}
+    t = timed(lambda: ops.gemm(h, wqkv, bias=bq, out=qkv, epilogue=L.WX_EPI_BF16))
+    res["gemm_qkv"] = {"s": t, "tflops": 2.0 * M * D * 3 * D / t / 1e12}
+    af = 4.0 * batch * CTX * CTX * D
+    t = timed(lambda: ops.attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], batch, N_HEAD,
+                                    0.125, out=o), reps=5)
+    res["attention"] = {"s": t, "tflops": af / t / 1e12}
+    lb = M * D * (4 + 2) + 2 * D * 4
+    t = timed(lambda: ops.layer_norm_rows(x, ones, zeros, out=hb, mode=L.WX_LN_FP32))
+    res["layernorm_f32_bf16"] = {"s": t, "gbs": lb / t / 1e9}
+    for k, v in res.items():
+        if "tflops" in v:
+            v["frac_of_measured_bf16"] = v["tflops"] * 1e12 / (peaks["bf16_tflops"] * 1e12)
+        else:
+            v["frac_of_measured_hbm"] = v["gbs"] / peaks["hbm_gbs"]
+    return res
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "src": "fallback"}
+
+
+def run_b200(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    from wxb200.encoder import Encoder
+
+    B = args.batch
+    W = make_weights_fast(seed=1)
+    enc = Encoder(W, max_batch=B, gelu="poly4")
+    del W
+    # per-clip seeded mel, pinned host copy for the end-to-end leg
+    g = torch.Generator().manual_seed(1000 + rank)
+    mel_host = torch.empty(B, N_MELS, 2 * CTX, pin_memory=True)
+    mel_host.copy_(torch.rand(B, N_MELS, 2 * CTX, generator=g) * 2.0 - 0.8)
+    out_host = torch.empty(B, CTX, D, pin_memory=True)
+    mel = mel_host.cuda()
+    out = torch.empty(B, CTX, D, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing
+    for _ in range(args.warmup):
+        enc.forward(mel, out=out)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(st)
+    for _ in range(args.steps):
+        enc.forward(mel, out=out)
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    finite = bool(torch.isfinite(out).all().item())
+
+    # ---- end to end through the public API, host buffers in and out
+    mel_np, out_np = mel_host.numpy(), out_host.numpy()
+    for _ in range(args.warmup):
+        enc.forward_host(mel_np, out=out_np)
+    torch.cuda.synchronize()
+    barrier()
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        enc.forward_host(mel_np, out=out_np)
+    t_e2e = max_over_ranks(time.perf_counter() - w0)
+    barrier()
+
+    total_clips = B * world * args.steps
+    value = total_clips / t_dev
+    e2e = total_clips / t_e2e
+    peaks = load_peaks()
+    roof, cpu = None, None
+    kernels = {}
+    if rank == 0:
+        kernels = kernel_rooflines(B, peaks)
+        k = kernels["gemm_fc1_gelu"]
+        fl = 2.0 * B * CTX * D * FFN
+        roof = {"bound": "tensor", "kernel": "gemm_bf16_kernel<256, BF16_GELU> (fc1 + GELU)",
+                "achieved": k["tflops"], "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": k["tflops"] / peaks["bf16_tflops"], "peak_source": peaks["src"],
+                "flop_per_launch": fl, "traffic": None,
+                "whole_step": {"achieved": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12,
+                               "frac": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12
+                               / peaks["bf16_tflops"]}}
+        if world == 1 and not args.no_cpu_baseline:
+            v, spent, desc = cpu_sample(args.cpu_layers)
+            cpu = {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
+                   "sample": desc + f"; {spent:.1f} s of CPU time"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t_dev / args.steps * 1e3,
+            "ms_per_clip_per_gpu": t_dev / args.steps * 1e3 / B,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (random N(0,0.02) large-v3 weights, "
+                                     "U[-0.8,1.2] log-mel per clip)",
+            "config": {"workload": f"large-v3 encoder forward, ctx 1500, {B} clips per GPU "
+                                   "per step (BASELINE batch-64 config, clip-sharded)",
+                       "model": "whisper large-v3 encoder (32 layers, d 1280, 20x64 heads, "
+                                "ffn 5120)",
+                       "global_batch": B * world, "seq_len": CTX,
+                       "parallelism": f"dp{world} (independent replicas, no collective)",
+                       "gelu": "poly4 RNE (the reference's device GELU)",
+                       "l2": "inputs larger than L2 (no flush)", "cuda_graph": True},
+            "e2e": {"value": e2e, "unit": UNIT,
+                    "h2d_bytes_per_step": int(mel_host.numel() * 4),
+                    "d2h_bytes_per_step": int(out_host.numel() * 4)},
+            "gpu_launches": (2 + 2 + 7 * N_LAYER + 1) * args.steps,
+            "roofline": roof, "kernels": kernels, "clocks": clk,
+            "cpu_baseline": cpu, "output_finite": finite,
+            "flop_per_clip": FLOP_PER_CLIP,
+        }
+        print(json.dumps(line), flush=True)
+    enc.close()
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,103 @@
+"""The whole encoder on the GPU against the CPU oracle.
+
+Tolerances (north star): cosine >= 0.9999 against the torch fp32 encoder at
+whisper-tiny depth, >= 0.99 at 32-layer large-v3 depth. The golden fixtures
+are outputs of the reference's own numpy path (tests/golden/make_golden.py),
+so the first test compares against the reference itself.
+"""
+import numpy as np
+import pytest
+import torch
+
+import encoder_ref as R
+from wxb200 import _lib as L
+from wxb200.encoder import Encoder, encoder
+from wxb200.runtime import B200RT
+
+from test_oracle import golden_case
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", ["tiny_l4_ctx128", "tiny_l2_ctx32_lnrand", "large_l1_ctx64"])
+@pytest.mark.parametrize("gelu", ["poly4", "erf"])
+def test_encoder_matches_reference_golden(cuda, name, gelu):
+    W, mel, nl, nh, ref = golden_case(name)
+    enc = Encoder(W, n_layer=nl, n_head=nh, gelu=gelu)
+    out = enc.forward_host(mel)
+    assert out.shape == ref.shape
+    assert R.cosine(out, ref) >= 0.9999, R.cosine(out, ref)
+
+
+@pytest.mark.parametrize("gelu", ["poly4", "erf"])
+def test_tiny_full_context_cosine(cuda, gelu):
+    """whisper-tiny, 4 layers, ctx 1500."""
+    W = R.make_weights("tiny", seed=1)
+    mel = R.make_mel(80, 3000, seed=0)
+    ref = R.encoder_torch(W, mel, 4, 6)
+    out = Encoder(W, gelu=gelu).forward_host(mel)
+    assert R.cosine(out, ref) >= 0.9999
+
+
+@pytest.mark.slow
+def test_large_v3_32_layers_cosine(cuda):
+    """large-v3, 32 layers, ctx 1500 (CPU oracle ~1 min)."""
+    W = R.make_weights("large-v3", seed=1)
+    mel = R.make_mel(128, 3000, seed=0)
+    out = Encoder(W, gelu="poly4").forward_host(mel)
+    ref = R.encoder_torch(W, mel, 32, 20)
+    assert R.cosine(out, ref) >= 0.99
+
+
+def test_batch_equals_single_clips_and_graph_replay(cuda):
+    """Clips in a batch are independent: batched output == per-clip output,
+    and graph replay == eager launches, bit for bit."""
+    W = R.make_weights("tiny", seed=2)
+    mels = np.stack([R.make_mel(80, 3000, seed=s) for s in range(3)])
+    enc = Encoder(W, max_batch=3)
+    batched = enc.forward_host(mels, use_graph=True)
+    again = enc.forward_host(mels, use_graph=True)
+    eager = enc.forward_host(mels, use_graph=False)
+    assert np.array_equal(batched, again) and np.array_equal(batched, eager)
+    for i in range(3):
+        assert np.array_equal(enc.forward_host(mels[i]), batched[i])
+
+
+def test_reduced_audio_ctx(cuda):
+    """audio_ctx 512: mel cut to 1024 frames (bench/run_raw_encoder.py:63-65)."""
+    W = R.make_weights("tiny", seed=3)
+    mel = R.make_mel(80, 1024, seed=4)
+    out = Encoder(W).forward_host(mel)
+    ref = R.encoder_torch(W, mel, 4, 6)
+    assert out.shape == (512, 384)
+    assert R.cosine(out, ref) >= 0.9999
+
+
+def test_device_forward_matches_host_forward(cuda):
+    W = R.make_weights("tiny", seed=5)
+    mel = R.make_mel(80, 3000, seed=6)
+    enc = Encoder(W)
+    host = enc.forward_host(mel)
+    dev = enc.forward(torch.from_numpy(mel).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(dev.cpu().numpy(), host)
+
+
+def test_dropin_encoder_signature(cuda):
+    """encoder(W, mel, RT.matmul, RT.matmul, ..., attn_fn=RT.attn_chain,
+    mlp_fn=RT.mlp, fold_bias=True) -- the server's call (serve/npu_stt_server.py:340-342)."""
+    W = R.add_transposed(R.make_weights("tiny", seed=1, n_layer=2))
+    mel = R.make_mel(80, 256, seed=0)
+    rt = B200RT()
+    prof = {}
+    out = encoder(W, mel, rt.matmul, rt.matmul, prof=prof, npu_softmax=False, n_layer=2,
+                  n_head=6, attn_fn=rt.attn_chain, mlp_fn=rt.mlp, fold_bias=True)
+    ref = R.encoder_np(W, mel, 2, 6)
+    assert out.shape == ref.shape and "total" in prof
+    assert R.cosine(out, ref) >= 0.9999
+    with pytest.raises(TypeError):
+        encoder(W, mel, R.mm, R.mm, n_layer=2, n_head=6)
+
+
+def test_no_device_error_recorded(cuda):
+    assert L.device_error() == 0

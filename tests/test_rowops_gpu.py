@@ -1,0 +1,184 @@
+"""Row ops on the GPU against the oracle, through the C ABI.
+
+Bar: bit-exact (the RNE and the truncating variants both: the oracle restates
+the reference kernels' rounding points and 16-lane summation order, and the
+exponential comes from the same host table). Shapes: the reference's own test
+shapes (tests/test_rowops.py), the BASELINE row-op sweep (GELU 1500x1536 and
+1500x5120, softmax 20x1500x1500 with scale 1/8, LayerNorm 1500x384 and
+1500x1280 with gamma/beta), windows, ragged widths, the +200 overflow rows.
+"""
+import numpy as np
+import pytest
+import torch
+
+import rowops_ref as O
+from wxb200 import _lib as L
+from wxb200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16_dev(x):
+    return torch.from_numpy(O.bf16_bits(x, O.RNE).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def host_f32(t):
+    t = t.contiguous().cpu()
+    if t.dtype == torch.bfloat16:
+        return (t.view(torch.int16).numpy().view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    return t.numpy()
+
+
+def bits_equal(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32),
+                          np.asarray(b, np.float32).view(np.uint32))
+
+
+def n_diff(a, b):
+    return int((np.asarray(a, np.float32).view(np.uint32) !=
+                np.asarray(b, np.float32).view(np.uint32)).sum())
+
+
+# ------------------------------------------------------------------ GELU
+
+@pytest.mark.parametrize("mode", [O.TRUNC, O.RNE])
+def test_gelu_every_bf16_value(cuda, mode):
+    x = O.bits_to_f32(np.arange(65536, dtype=np.uint32).astype(np.uint16)).reshape(256, 256)
+    finite = np.isfinite(x)
+    x = np.where(finite, x, 0).astype(np.float32)
+    got = host_f32(ops.gelu_poly4(bf16_dev(x), rounding=mode))
+    assert bits_equal(got, O.gelu_poly4(x, mode))
+
+
+@pytest.mark.parametrize("shape", [(1500, 1536), (1500, 5120), (7, 13), (3, 1000)])
+@pytest.mark.parametrize("mode", [O.TRUNC, O.RNE])
+def test_gelu_bf16_shapes(cuda, shape, mode):
+    rng = np.random.default_rng(shape[1])
+    x = O.rbf((3 * rng.standard_normal(shape)).astype(np.float32), O.RNE)
+    got = host_f32(ops.gelu_poly4(bf16_dev(x), rounding=mode))
+    assert bits_equal(got, O.gelu_poly4(x, mode))
+
+
+@pytest.mark.parametrize("shape", [(1500, 1536), (1500, 5120), (5, 37)])
+def test_gelu_f32_input_g4f(cuda, shape):
+    rng = np.random.default_rng(7)
+    x = (3 * rng.standard_normal(shape)).astype(np.float32)
+    got = host_f32(ops.gelu_poly4(torch.from_numpy(x).cuda(), rounding=O.RNE))
+    assert bits_equal(got, O.gelu_row4f(x))
+
+
+def test_gelu_f32_band_into_wider_buffer(cuda):
+    """g4f writing column band j of fc2's input (src/rawxrt.py:505-516)."""
+    rng = np.random.default_rng(8)
+    rows, w, nb = 1500, 1280, 4
+    big = torch.zeros(rows, w * nb, dtype=torch.bfloat16, device="cuda")
+    xs = [(3 * rng.standard_normal((rows, w))).astype(np.float32) for _ in range(nb)]
+    for j, x in enumerate(xs):
+        ops.gelu_poly4(torch.from_numpy(x).cuda(), out=big[:, j * w:(j + 1) * w])
+    got = host_f32(big)
+    for j, x in enumerate(xs):
+        assert bits_equal(got[:, j * w:(j + 1) * w], O.gelu_row4f(x))
+
+
+# ------------------------------------------------------------------ softmax
+
+@pytest.mark.parametrize("variant,mode", [(4, O.TRUNC), (4, O.RNE), (1, O.TRUNC),
+                                          (3, O.TRUNC), (3, O.RNE), (1, O.RNE)])
+@pytest.mark.parametrize("shape,valid", [((96, 1536), 0), ((96, 1536), 1504), ((64, 512), 0),
+                                         ((33, 1500), 0), ((17, 100), 93), ((8, 7), 0)])
+def test_softmax_variants(cuda, variant, mode, shape, valid):
+    rng = np.random.default_rng(shape[0] * 7 + valid)
+    x = O.rbf(rng.normal(0, 6, shape).astype(np.float32), O.RNE)
+    out = torch.full(shape, 3.0, dtype=torch.bfloat16, device="cuda")
+    ops.softmax_rows(bf16_dev(x), out=out, valid=valid, variant=variant, rounding=mode)
+    got = host_f32(out)
+    w = valid if valid > 0 else shape[1]
+    assert bits_equal(got[:, :w], O.softmax_row(x, mode=mode, variant=variant, valid=valid))
+    assert np.all(got[:, w:] == 3.0)  # outside the window: neither read nor written
+
+
+def test_softmax_baseline_shape_with_scale(cuda):
+    """BASELINE row-op config: 20 x 1500 x 1500 scores, scale 1/8."""
+    rng = np.random.default_rng(11)
+    x = O.rbf((3 * rng.standard_normal((20 * 1500, 1500))).astype(np.float32), O.RNE)
+    got = host_f32(ops.softmax_rows(bf16_dev(x), scale=0.125, variant=4, rounding=O.RNE))
+    ref = O.softmax_row(x, mode=O.RNE, variant=4, scale=0.125)
+    assert bits_equal(got, ref)
+
+
+@pytest.mark.parametrize("rows,cols", [(10240, 512), (9216, 1536)])
+def test_softmax_reference_test_shapes(cuda, rows, cols):
+    """tests/test_rowops.py:35-53: N(0,6) logits, rel L2 < 0.02 and finite --
+    and bit-exact to the oracle."""
+    rng = np.random.default_rng(0)
+    x = O.rbf(rng.normal(0, 6.0, (rows, cols)).astype(np.float32), O.RNE)
+    got = host_f32(ops.softmax_rows(bf16_dev(x), variant=1, rounding=O.TRUNC))
+    assert bits_equal(got, O.softmax_row(x, mode=O.TRUNC, variant=1))
+    ref = O.softmax_fp32(x)
+    assert np.isfinite(got).all() and np.linalg.norm(got - ref) / np.linalg.norm(ref) < 0.02
+
+
+def test_softmax_overflow_rows(cuda):
+    rng = np.random.default_rng(0)
+    x = O.rbf((rng.normal(0, 6.0, (512, 512)) + 200.0).astype(np.float32), O.RNE)
+    for variant in (1, 3, 4):
+        got = host_f32(ops.softmax_rows(bf16_dev(x), variant=variant, rounding=O.TRUNC))
+        assert bits_equal(got, O.softmax_row(x, mode=O.TRUNC, variant=variant))
+        assert np.isfinite(got).all()
+
+
+def test_softmax_strided_rows(cuda):
+    """Rows read from and written into wider buffers (row stride != width)."""
+    rng = np.random.default_rng(5)
+    x = O.rbf(rng.normal(0, 4, (40, 200)).astype(np.float32), O.RNE)
+    src = bf16_dev(x)
+    dst = torch.zeros(40, 256, dtype=torch.bfloat16, device="cuda")
+    ops.softmax_rows(src[:, 8:168], out=dst[:, 16:176], variant=4, rounding=O.RNE)
+    got = host_f32(dst)
+    assert bits_equal(got[:, 16:176], O.softmax_row(x[:, 8:168], mode=O.RNE, variant=4))
+    assert np.all(got[:, :16] == 0) and np.all(got[:, 176:] == 0)
+
+
+# ------------------------------------------------------------------ LayerNorm
+
+@pytest.mark.parametrize("mode", [O.TRUNC, O.RNE])
+@pytest.mark.parametrize("rows,cols", [(512, 1280), (1536, 384), (1500, 384), (1500, 1280),
+                                       (9, 40)])
+def test_layernorm_aie(cuda, mode, rows, cols):
+    rng = np.random.default_rng(rows + cols)
+    x = O.rbf(rng.normal(0.3, 1.0, (rows, cols)).astype(np.float32), O.RNE)
+    got = host_f32(ops.layer_norm_rows(bf16_dev(x), mode=L.WX_LN_AIE, rounding=mode))
+    assert bits_equal(got, O.layer_norm_aie(x, mode))
+
+
+@pytest.mark.parametrize("rows,cols", [(1500, 384), (1500, 1280)])
+def test_layernorm_aie_gamma_beta(cuda, rows, cols):
+    """BASELINE: LayerNorm with gamma ~ 1 + N(0, 0.1), beta ~ N(0, 0.1)."""
+    rng = np.random.default_rng(cols)
+    x = O.rbf((3 * rng.standard_normal((rows, cols))).astype(np.float32), O.RNE)
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(cols)).astype(np.float32)
+    got = host_f32(ops.layer_norm_rows(bf16_dev(x), gamma=torch.from_numpy(g).cuda(),
+                                       beta=torch.from_numpy(b).cuda(), mode=L.WX_LN_AIE,
+                                       rounding=O.RNE))
+    assert bits_equal(got, O.layer_norm_aie(x, O.RNE, gamma=g, beta=b))
+
+
+@pytest.mark.parametrize("cols", [384, 1280, 4096])
+@pytest.mark.parametrize("out_bf16", [True, False])
+def test_layernorm_fp32_mode(cuda, cols, out_bf16):
+    """The encoder's LayerNorm (src/npu_whisper_encoder.py:278-281) in fp32."""
+    rng = np.random.default_rng(cols)
+    x = (rng.normal(0.5, 2.0, (300, cols))).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(cols)).astype(np.float32)
+    got = host_f32(ops.layer_norm_rows(torch.from_numpy(x).cuda(), torch.from_numpy(g).cuda(),
+                                       torch.from_numpy(b).cuda(), mode=L.WX_LN_FP32,
+                                       out_dtype=torch.bfloat16 if out_bf16 else torch.float32))
+    ref = O.layer_norm_host(x, g, b)
+    tol = 2 ** -8 if out_bf16 else 1e-5
+    assert np.max(np.abs(got - ref) / (np.abs(ref) + 1e-3)) < tol
+
+
+def test_no_device_error_recorded(cuda):
+    assert L.device_error() == 0

@@ -1,0 +1,288 @@
+// Shared device helpers for the sm_100a kernels: bf16 rounding in the two AIE
+// modes, bounded mbarrier waits, TMA loads and the tcgen05 (5th-generation
+// tensor core) instructions, all as inline PTX.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "wxb200_internal.h"
+
+namespace wx {
+
+// ---------------------------------------------------------------- rounding
+// Rounding modes of the reference's AIE2 kernels: RND_TRUNC is the part's
+// default (truncate toward zero), RND_RNE is aie::set_rounding(conv_even).
+enum { RND_TRUNC = 0, RND_RNE = 1 };
+
+template <int R>
+__device__ __forceinline__ uint32_t bf16_bits(float x) {
+  if (R == RND_TRUNC) return __float_as_uint(x) >> 16;
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+__device__ __forceinline__ float bits_f32(uint32_t b) { return __uint_as_float(b << 16); }
+
+// Round an fp32 value to a bf16-representable fp32 value.
+template <int R>
+__device__ __forceinline__ float rbf(float x) {
+  if (R == RND_TRUNC) return __uint_as_float(__float_as_uint(x) & 0xFFFF0000u);
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Two fp32 -> packed bf16x2 (lo in the low half), RNE.
+__device__ __forceinline__ uint32_t pack_bf16x2_rne(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <int R>
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  if (R == RND_RNE) return pack_bf16x2_rne(lo, hi);
+  return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
+}
+
+// ---------------------------------------------------------------- GELU poly4
+// The piecewise degree-4 erf-GELU of the reference (kernels/gelu_poly4_eval.inc
+// :27-65). Its table (kernels/gelu_poly4_coeffs.h:6-13) is used the way the
+// kernels use it, every entry cast (bfloat16)float at its point of use; the
+// decimal literals there round to the same bf16 values in both rounding
+// modes, and those bf16 values are spelled out here exactly, so the device
+// code selects between immediates. (rowops.cu rounds the decimal literals on
+// the host and a CPU test checks both against the oracle.)
+struct Gelu4Table {
+  float brk[3], shift[3], scale[3], c[3][5];
+};
+
+// Host: the table rounded to bf16 in mode R from the decimal literals (rowops.cu).
+Gelu4Table gelu4_table(int mode);
+
+// breaks {1, 2, 4}, shifts {0.5, 1.5, 3}, scales {2, 2, 1}
+#define WX_GELU4_COEF                                                                  \
+  {{-0x1.0cp-9f, -0x1.aap-7f, 0x1.3cp-4f, -0x1.1p-4f, -0x1.3cp-3f},                    \
+   {0x1.1ap-9f, -0x1.d6p-8f, -0x1.08p-8f, 0x1.06p-4f, -0x1.9ap-4f},                    \
+   {-0x1.8p-9f, 0x1.5ep-7f, -0x1.04p-6f, 0x1.8ap-7f, -0x1.08p-8f}}
+
+template <int R>
+__device__ __forceinline__ float gelu_poly4(float x) {
+  constexpr float kC[3][5] = WX_GELU4_COEF;
+  // x holds a bf16 value. s = max(x, 0 - x)
+  const float s = fabsf(x);
+  const bool p0 = s < 1.0f, p1 = s < 2.0f, p2 = s < 4.0f;
+  float q = 0.0f;
+  if (p2) {  // the innermost piece with s < break wins (:40-61)
+    const float sh = p0 ? 0.5f : (p1 ? 1.5f : 3.0f);
+    const float sc = p2 && !p1 ? 1.0f : 2.0f;
+    float c[5];
+#pragma unroll
+    for (int k = 0; k < 5; k++) c[k] = p0 ? kC[0][k] : (p1 ? kC[1][k] : kC[2][k]);
+    const float u = rbf<R>(rbf<R>(s - sh) * sc);     // bf16 sub, bf16 mul
+    float acc = c[0];
+#pragma unroll
+    for (int k = 1; k < 5; k++) acc = fmaf(rbf<R>(acc), u, c[k]);  // exact product
+    q = rbf<R>(acc);
+  }
+  const float relu = (x >= 0.0f) ? x : 0.0f;          // aie::max(x, zero)
+  return rbf<R>(relu + q);
+}
+
+// 2^x on the SFU (MUFU.EX2), flushing denormal results; 2^-inf = +0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ---------------------------------------------------------------- timers
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Every spin-wait in these kernels gives up after this long, records
+// WX_DEVERR_TIMEOUT in the device error word and lets the kernel return.
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+
+__device__ __forceinline__ void set_device_error(int* err, int code) {
+  if (err) atomicOr(err, code);
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait with an explicit time limit and no error reporting (used to drain copies
+// still in flight on a bail-out path).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer_ns() - t0 > ns) return false;
+  return true;
+}
+
+// Wait for the phase with the given parity to complete. Bounded: returns false
+// (and records a timeout) if it has not after kWaitTimeoutNs, or at once if
+// another thread of this kernel has already recorded an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; i++)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (err && *reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      set_device_error(err, WX_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- TMA
+// 2-D tiled bulk tensor load into this CTA's shared memory, completing on an
+// mbarrier. x is the innermost (contiguous) coordinate in elements; callers
+// keep x * sizeof(element) a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// generic-proxy shared-memory writes -> visible to the async proxy (tcgen05.mma)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 in, fp32 accumulate.
+__device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on an mbarrier once every tcgen05.mma issued so far by this thread
+// has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets row
+// (lane base + i), columns [col, col + 32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+      "[%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Shared-memory matrix descriptor for a K-major operand stored as TMA writes it
+// with 128-byte swizzling: rows of 128 bytes, 8-row groups 1024 bytes apart.
+// Fields: start address >> 4 [0,14), leading byte offset >> 4 [16,30) (unused
+// for swizzled K-major), stride byte offset >> 4 [32,46), version 1 [46,48),
+// layout type SWIZZLE_128B = 2 [61,64).
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// The same layout read MN-major (the contiguous 128-byte rows run along N):
+// one 64-element atom along N, 8-row K groups 1024 bytes apart (stride byte
+// offset); the leading byte offset would step between N atoms.
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), bf16 A
+// and B (bits 7-9, 10-12 = 1), A/B major (bits 15, 16), N >> 3 (bits 17-22),
+// M >> 4 (bits 24-28).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn_major,
+                                                      int b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn_major << 15) |
+         ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+}  // namespace wx

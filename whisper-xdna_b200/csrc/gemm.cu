@@ -1,0 +1,402 @@
+// bf16 GEMM with fp32 accumulation on the sm_100a tensor cores (tcgen05) and
+// fused epilogues: the QKV / out-proj / fc1 / fc2 / conv GEMMs of the encoder.
+//
+//   C = epilogue(A @ B^T), A (M x K) bf16 row-major, B (N x K) bf16 row-major
+//   (the torch Linear weight), fp32 accumulator in tensor memory.
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0     TMA producer: A and B tiles (128 x 64 and BN x 64 bf16, 128-byte
+//              swizzle) into a STAGES-deep shared-memory ring
+//   warp 1     allocates tensor memory and issues tcgen05.mma (M=128, N=BN,
+//              K=16 per instruction) from one thread; tcgen05.commit frees the
+//              ring slot and publishes the finished accumulator
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//              32*(w%4)...), bias / residual / GELU, bf16 or fp32 stores
+// The accumulator is double-buffered in tensor memory (2 x BN columns), so the
+// epilogue of one tile overlaps the MMAs of the next. Tiles are visited
+// N-fastest so the CTAs in flight share A tiles through L2; the weights
+// (<= 13 MB per GEMM) stay L2-resident.
+//
+// It replaces the whole-array AIE GEMM the reference drives through
+// RawRT.matmul / mm_start / mm_finish (src/rawxrt.py:926-996); its bias fold
+// (ones column on A, bias row on B, src/rawxrt.py:352-371) becomes a bias
+// added to the fp32 accumulator in the epilogue.
+#include "common.cuh"
+#include "plans.cuh"
+
+namespace wx {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
+  static constexpr int B_BYTES = BN * kGemmBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+// Apply the epilogue to 32 consecutive accumulator columns of one row and
+// store them. `full` = all 32 columns are inside N and the stores may be
+// vectorized.
+template <int EPI>
+__device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int row, int n, bool full,
+                                                 const uint32_t (&acc)[32]) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) v[j] = __uint_as_float(acc[j]);
+  if (a.bias) {
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(a.bias + n + j));
+        v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n + j < a.N) v[j] += a.bias[n + j];
+    }
+  }
+  if (EPI == WX_EPI_F32_RESID) {
+    const float* r = a.R + (int64_t)row * a.ldr + n;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(r + j);
+        v[j] += t.x; v[j + 1] += t.y; v[j + 2] += t.z; v[j + 3] += t.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n + j < a.N) v[j] += r[j];
+    }
+  }
+  if (EPI == WX_EPI_BF16_GELU || EPI == kEpiF32GeluPos) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = gelu_poly4<RND_RNE>(rbf<RND_RNE>(v[j]));
+  }
+  if (EPI == WX_EPI_BF16_GELU_ERF || EPI == kEpiF32GeluErfPos) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = gelu_erf(v[j]);
+  }
+  if (EPI == kEpiF32GeluPos || EPI == kEpiF32GeluErfPos) {
+    const float* pp = a.pos + (int64_t)(row % a.pos_T) * a.ldp + n;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(pp + j));
+        v[j] += t.x; v[j + 1] += t.y; v[j + 2] += t.z; v[j + 3] += t.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n + j < a.N) v[j] += pp[j];
+    }
+  }
+  if (EPI == WX_EPI_F32 || EPI == WX_EPI_F32_RESID || EPI == kEpiF32GeluPos ||
+      EPI == kEpiF32GeluErfPos) {
+    float* c = reinterpret_cast<float*>(a.C) + (int64_t)row * a.ldc + n;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n + j < a.N) c[j] = v[j];
+    }
+  } else {
+    uint16_t* c = reinterpret_cast<uint16_t*>(a.C) + (int64_t)row * a.ldc + n;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 o;
+        o.x = pack_bf16x2_rne(v[j], v[j + 1]);
+        o.y = pack_bf16x2_rne(v[j + 2], v[j + 3]);
+        o.z = pack_bf16x2_rne(v[j + 4], v[j + 5]);
+        o.w = pack_bf16x2_rne(v[j + 6], v[j + 7]);
+        *reinterpret_cast<uint4*>(c + j) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (n + j < a.N) c[j] = (uint16_t)bf16_bits<RND_RNE>(v[j]);
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nnb = a.num_n_blocks, nkb = a.num_k_blocks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued = 0, issued_phase = 0;  // per-slot bits
+      for (int tile = blockIdx.x; ok && tile < a.num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / nnb) * kGemmBM, n0 = (tile % nnb) * BN;
+        for (int kb = 0; kb < nkb; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, a.err)) { ok = false; break; }
+          issued |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(&tmA, &full[stage], sA + stage * Cfg::A_BYTES, kb * kGemmBK, m0);
+          tma_load_2d(&tmB, &full[stage], sB + stage * Cfg::B_BYTES, kb * kGemmBK, n0);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Loads still in flight land before the CTA retires: wait (1 ms at most
+      // per slot) for the slots the MMA warp will no longer consume.
+      if (!ok)
+        for (int s = 0; s < S; s++)
+          if (issued & (1u << s)) mbar_wait_for(&full[s], (issued_phase >> s) & 1u, 1000000ull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = idesc_bf16_f32(kGemmBM, BN, 0, 0);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < a.num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, a.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nkb; kb++) {
+          if (!mbar_wait(&full[stage], phase, a.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; k++)
+            umma_bf16_ss(d_tmem, sdesc_kmajor_sw128(a_base + k * 32),
+                         sdesc_kmajor_sw128(b_base + k * 32), idesc, (kb | k) != 0);
+          umma_commit(&empty[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // every MMA issued has completed before tensor memory is released
+      umma_commit(done);
+      mbar_wait_for(done, 0, kWaitTimeoutNs);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5
+    const int sub = warp & 3;  // TMEM lanes 32*sub .. 32*sub+31
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x) {
+      const int m0 = (tile / nnb) * kGemmBM, n0 = (tile % nnb) * BN;
+      if (!mbar_wait(&tfull[acc], acc_phase, a.err)) break;
+      tc_fence_after();
+      const int row = m0 + sub * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        const int n = n0 + c * 32;
+        if (n >= a.N) break;  // uniform across the warp
+        uint32_t r[32];
+        tmem_ld32(t_row + (uint32_t)(c * 32), r);
+        tmem_wait_ld();
+        if (row < a.M) epilogue_store32<EPI>(a, row, n, n + 32 <= a.N, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+static int gemm_prepare(int bn, int epi);
+
+// Build the tensor maps and launch arguments once; the encoder keeps plans for
+// its fixed buffers, the standalone entry point builds one per call.
+int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, const float* R,
+              void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+              int64_t ldr, int epi, int force_bn) {
+  if (M <= 0 || N <= 0 || K <= 0) return fail(WX_ERR_INVALID, "gemm: M, N, K must be > 0");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(WX_ERR_UNSUPPORTED, "gemm: dimension exceeds 2^31");
+  if (!A || !B || !C) return fail(WX_ERR_INVALID, "gemm: NULL operand");
+  const bool pos_epi = epi == kEpiF32GeluPos || epi == kEpiF32GeluErfPos;
+  if ((epi < WX_EPI_F32 || epi > WX_EPI_BF16_GELU_ERF) && !pos_epi)
+    return fail(WX_ERR_INVALID, "gemm: epilogue %d", epi);
+  if (epi == WX_EPI_F32_RESID && !R) return fail(WX_ERR_INVALID, "gemm: residual is NULL");
+  if (lda < K || ldb < K || ldc < N) return fail(WX_ERR_INVALID, "gemm: leading dimension too small");
+  if (lda % 8 || ldb % 8) return fail(WX_ERR_INVALID, "gemm: lda and ldb must be multiples of 8");
+  const bool f32_out = epi == WX_EPI_F32 || epi == WX_EPI_F32_RESID || pos_epi;
+  if (ldc % (f32_out ? 4 : 8)) return fail(WX_ERR_INVALID, "gemm: ldc must keep rows 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(C) & 15) || (bias && (reinterpret_cast<uintptr_t>(bias) & 15)))
+    return fail(WX_ERR_INVALID, "gemm: C and bias must be 16-byte aligned");
+  if (R && ((reinterpret_cast<uintptr_t>(R) & 15) || ldr % 4 || ldr < N))
+    return fail(WX_ERR_INVALID, "gemm: residual must be 16-byte aligned with ldr a multiple of 4");
+  const int nsm = sm_count();
+  const int64_t mb = (M + kGemmBM - 1) / kGemmBM;
+  int bn = force_bn;
+  if (bn == 0) bn = (mb * ((N + 255) / 256) >= nsm && N > 128) ? 256 : 128;
+  if (bn != 128 && bn != 256) return fail(WX_ERR_INVALID, "gemm: BN %d", bn);
+  int* err = device_error_word();
+  if (!err) return fail(WX_ERR_CUDA, "gemm: device error word unavailable");
+  WX_TRY(encode_tensor_map_2d(&p->tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
+                              (uint64_t)M, (uint64_t)lda * 2, kGemmBK, kGemmBM,
+                              CU_TENSOR_MAP_SWIZZLE_128B));
+  WX_TRY(encode_tensor_map_2d(&p->tmB, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
+                              (uint64_t)N, (uint64_t)ldb * 2, kGemmBK, (uint32_t)bn,
+                              CU_TENSOR_MAP_SWIZZLE_128B));
+  GemmArgs& g = p->args;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.num_n_blocks = (int)((N + bn - 1) / bn);
+  g.num_tiles = (int)(mb * g.num_n_blocks);
+  g.num_k_blocks = (int)((K + kGemmBK - 1) / kGemmBK);
+  g.C = C;
+  g.ldc = ldc;
+  g.bias = bias;
+  g.R = R;
+  g.ldr = ldr;
+  g.err = err;
+  g.pos = nullptr;
+  g.ldp = 0;
+  g.pos_T = 1;
+  p->bn = bn;
+  p->epi = epi;
+  p->grid = g.num_tiles < nsm ? g.num_tiles : nsm;
+  return gemm_prepare(bn, epi);
+}
+
+template <int BN, int EPI>
+static int set_attr_t() {
+  static bool done[64] = {false};
+  int dev = 0;
+  WX_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 64 && done[dev]) return WX_OK;
+  WX_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_kernel<BN, EPI>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM));
+  if (dev < 64) done[dev] = true;
+  return WX_OK;
+}
+
+template <int BN, int EPI>
+static int launch_t(const GemmPlan& p, cudaStream_t st) {
+  gemm_bf16_kernel<BN, EPI><<<p.grid, 192, GemmCfg<BN>::SMEM, st>>>(p.tmA, p.tmB, p.args);
+  return check_launch("gemm_bf16");
+}
+
+// Kernel attributes are set when a plan is made, so that a captured launch
+// sequence contains nothing but launches.
+static int gemm_prepare(int bn, int epi) {
+#define WX_GEMM_PREP(E) \
+  case E:               \
+    return bn == 256 ? set_attr_t<256, E>() : set_attr_t<128, E>();
+  switch (epi) {
+    WX_GEMM_PREP(WX_EPI_F32)
+    WX_GEMM_PREP(WX_EPI_BF16)
+    WX_GEMM_PREP(WX_EPI_F32_RESID)
+    WX_GEMM_PREP(WX_EPI_BF16_GELU)
+    WX_GEMM_PREP(WX_EPI_BF16_GELU_ERF)
+    WX_GEMM_PREP(kEpiF32GeluPos)
+    WX_GEMM_PREP(kEpiF32GeluErfPos)
+    default:
+      return fail(WX_ERR_INVALID, "gemm: epilogue %d", epi);
+  }
+#undef WX_GEMM_PREP
+}
+
+int gemm_run(const GemmPlan& p, cudaStream_t st) {
+#define WX_GEMM_CASE(E)                                               \
+  case E:                                                             \
+    return p.bn == 256 ? launch_t<256, E>(p, st) : launch_t<128, E>(p, st);
+  switch (p.epi) {
+    WX_GEMM_CASE(WX_EPI_F32)
+    WX_GEMM_CASE(WX_EPI_BF16)
+    WX_GEMM_CASE(WX_EPI_F32_RESID)
+    WX_GEMM_CASE(WX_EPI_BF16_GELU)
+    WX_GEMM_CASE(WX_EPI_BF16_GELU_ERF)
+    WX_GEMM_CASE(kEpiF32GeluPos)
+    WX_GEMM_CASE(kEpiF32GeluErfPos)
+    default:
+      return fail(WX_ERR_INVALID, "gemm: epilogue %d", p.epi);
+  }
+#undef WX_GEMM_CASE
+}
+
+void gemm_set_pos(GemmPlan* p, const float* pos, int64_t ldp, int pos_T) {
+  p->args.pos = pos;
+  p->args.ldp = ldp;
+  p->args.pos_T = pos_T;
+}
+
+}  // namespace wx
+
+extern "C" {
+
+int wx_gemm_bf16(const void* A, const void* B, const float* bias, const float* R, void* C,
+                 int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                 int64_t ldr, int epilogue, void* stream) {
+  wx::GemmPlan p;
+  WX_TRY(wx::gemm_plan(&p, A, B, bias, R, C, M, N, K, lda, ldb, ldc, ldr, epilogue, 0));
+  return wx::gemm_run(p, wx::as_stream(stream));
+}
+
+}  // extern "C"

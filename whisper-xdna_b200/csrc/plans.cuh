@@ -1,0 +1,72 @@
+// Launch plans shared between the standalone entry points and the encoder:
+// tensor maps and kernel arguments built once for fixed buffers.
+#pragma once
+#include "common.cuh"
+
+namespace wx {
+
+struct GemmArgs {
+  int M, N, K;
+  int num_n_blocks, num_tiles, num_k_blocks;
+  void* C;
+  int64_t ldc;
+  const float* bias;
+  const float* R;
+  int64_t ldr;
+  int* err;
+  const float* pos;  // positional embedding (WX_EPI_*_POS), row (row % pos_T)
+  int64_t ldp;
+  int pos_T;
+};
+
+// Epilogues used only inside the library (the conv2 step of the encoder):
+//   C fp32 = GELU(acc + bias) + pos[row % pos_T]
+constexpr int kEpiF32GeluPos = 16;     // GELU = poly4 RNE on rne(acc + bias)
+constexpr int kEpiF32GeluErfPos = 17;  // GELU = exact erf form
+
+struct GemmPlan {
+  CUtensorMap tmA, tmB;
+  GemmArgs args;
+  int bn;
+  int grid;
+  int epi;
+};
+
+// force_bn: 0 = pick, else 128 or 256 (output columns per tile)
+int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, const float* R,
+              void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+              int64_t ldr, int epi, int force_bn);
+int gemm_run(const GemmPlan& p, cudaStream_t st);
+// attach the positional embedding to a plan built with kEpiF32Gelu*Pos
+void gemm_set_pos(GemmPlan* p, const float* pos, int64_t ldp, int pos_T);
+
+struct AttnArgs {
+  int T, H, num_q_tiles;
+  void* O;
+  int64_t ldo;
+  float scale_log2;
+  int* err;
+};
+
+struct AttnPlan {
+  CUtensorMap tmQ, tmK, tmV;
+  AttnArgs args;
+  int B;
+};
+
+int attn_plan(AttnPlan* p, const void* q, const void* k, const void* v, void* o, int64_t B,
+              int64_t H, int64_t T, int64_t hd, int64_t ldq, int64_t ldk, int64_t ldv,
+              int64_t ldo, float scale);
+int attn_run(const AttnPlan& p, cudaStream_t st);
+
+// row ops (rowops.cu)
+int launch_gelu_poly4(const void* in, int in_dtype, void* out, int64_t rows, int64_t cols,
+                      int64_t ld_in, int64_t ld_out, int rounding, cudaStream_t st);
+int launch_softmax_rows(const void* in, void* out, int64_t rows, int64_t cols, int64_t valid,
+                        int64_t ld_in, int64_t ld_out, float scale, int variant, int rounding,
+                        cudaStream_t st);
+int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, const float* beta,
+                          void* out, int out_dtype, int64_t rows, int64_t cols, int64_t ld_in,
+                          int64_t ld_out, float eps, int mode, int rounding, cudaStream_t st);
+
+}  // namespace wx

@@ -1,0 +1,671 @@
+// Row ops of the Whisper-encoder hot path as bandwidth-bound sm_100a kernels:
+// polynomial GELU (g4 / g4r / g4f), row softmax (v1 / v3 / v4, windowed, with
+// an optional input scale) and LayerNorm (the reference's device arithmetic,
+// and the fp32 host form the encoder uses).
+//
+// The bf16 rounding points, the 16-lane summation order and the constant
+// tables follow the reference's AIE2 kernels exactly, so the RNE variants are
+// bit-exact to the CPU restatement:
+//   GELU     kernels/gelu_poly4_eval.inc:27-65, kernels/gelu_poly4_coeffs.h:6-13
+//   softmax  kernels/softmax_row4_body.inc:17-60, softmax_row.cc:25-59,
+//            softmax_row3.cc:34-86, windowing src/rowops.py:60-73
+//   LN       kernels/layer_norm_gb.cc:22-85
+// Memory access: 16-byte vector loads and stores, rows staged in shared memory
+// so HBM is read and written once.
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace wx {
+
+// ---------------------------------------------------------------- host tables
+// The reference's GELU table (kernels/gelu_poly4_coeffs.h:6-13), consumed as
+// constants: breaks, shifts, scales and the degree-4 coefficients of each of
+// the three pieces, highest degree first.
+static const float kGeluBreak[3] = {1.000000f, 2.000000f, 4.000000f};
+static const float kGeluShift[3] = {0.500000f, 1.500000f, 3.000000f};
+static const float kGeluScale[3] = {2.000000f, 2.000000f, 1.000000f};
+static const float kGeluCoef[3][5] = {
+    {-0.0020446777f, -0.013000488f, 0.077148438f, -0.06640625f, -0.15429688f},
+    {0.0021514893f, -0.0071716309f, -0.0040283203f, 0.063964844f, -0.10009766f},
+    {-0.0029296875f, 0.010681152f, -0.015869141f, 0.012023926f, -0.0040283203f},
+};
+
+static inline uint32_t h_f2u(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+static inline float h_u2f(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+uint16_t host_bf16_bits(float f, int mode) {
+  uint32_t u = h_f2u(f);
+  if (std::isnan(f)) return (uint16_t)((u >> 16) | 0x40);
+  if (mode == RND_TRUNC) return (uint16_t)(u >> 16);
+  uint32_t bias = ((u >> 16) & 1u) + 0x7FFFu;
+  return (uint16_t)((uint64_t(u) + bias) >> 16);
+}
+float host_rbf(float f, int mode) { return h_u2f(uint32_t(host_bf16_bits(f, mode)) << 16); }
+
+Gelu4Table gelu4_table(int mode) {
+  Gelu4Table t;
+  for (int p = 0; p < 3; p++) {
+    t.brk[p] = host_rbf(kGeluBreak[p], mode);
+    t.shift[p] = host_rbf(kGeluShift[p], mode);
+    t.scale[p] = host_rbf(kGeluScale[p], mode);
+    for (int k = 0; k < 5; k++) t.c[p][k] = host_rbf(kGeluCoef[p][k], mode);
+  }
+  return t;
+}
+
+// exp of every bf16 x' in [-128, -0]: bit patterns [0x8000, 0xC300). Below -128
+// the exponential is 0 in fp32 and bf16; x' = +0 gives 1.
+constexpr int kExpTabBase = 0x8000;
+constexpr int kExpTabN = 0xC300 - 0x8000;
+
+static void host_exp_tables(uint16_t* t16_trunc, uint16_t* t16_rne, float* t32) {
+  for (int i = 0; i < kExpTabN; i++) {
+    float x = h_u2f(uint32_t(kExpTabBase + i) << 16);
+    float e = (float)std::exp((double)x);
+    t32[i] = e;
+    t16_trunc[i] = host_bf16_bits(e, RND_TRUNC);
+    t16_rne[i] = host_bf16_bits(e, RND_RNE);
+  }
+}
+
+struct ExpTablesDev {
+  uint16_t* t16[2] = {nullptr, nullptr};
+  float* t32 = nullptr;
+};
+
+static std::mutex g_tab_mu;
+static ExpTablesDev g_tabs[64];
+
+static int exp_tables(ExpTablesDev** out) {
+  int dev = 0;
+  WX_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 64) return fail(WX_ERR_UNSUPPORTED, "device index %d >= 64", dev);
+  std::lock_guard<std::mutex> lk(g_tab_mu);
+  ExpTablesDev& t = g_tabs[dev];
+  if (!t.t32) {
+    std::vector<uint16_t> a(kExpTabN), b(kExpTabN);
+    std::vector<float> c(kExpTabN);
+    host_exp_tables(a.data(), b.data(), c.data());
+    WX_CUDA_TRY(cudaMalloc(&t.t16[0], kExpTabN * 2));
+    WX_CUDA_TRY(cudaMalloc(&t.t16[1], kExpTabN * 2));
+    WX_CUDA_TRY(cudaMalloc(&t.t32, kExpTabN * 4));
+    WX_CUDA_TRY(cudaMemcpy(t.t16[0], a.data(), kExpTabN * 2, cudaMemcpyHostToDevice));
+    WX_CUDA_TRY(cudaMemcpy(t.t16[1], b.data(), kExpTabN * 2, cudaMemcpyHostToDevice));
+    WX_CUDA_TRY(cudaMemcpy(t.t32, c.data(), kExpTabN * 4, cudaMemcpyHostToDevice));
+  }
+  *out = &t;
+  return WX_OK;
+}
+
+// ---------------------------------------------------------------- GELU
+template <int R, bool F32IN, int VEC>
+__global__ void __launch_bounds__(256) gelu_poly4_kernel(const void* __restrict__ in,
+                                                         uint16_t* __restrict__ out,
+                                                         int64_t rows, int64_t cols,
+                                                         int64_t ld_in, int64_t ld_out) {
+  const int64_t per_row = cols / VEC;
+  const int64_t total = rows * per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / per_row;
+    const int64_t c = (i - r * per_row) * VEC;
+    float x[VEC];
+    if (F32IN) {
+      const float* src = reinterpret_cast<const float*>(in) + r * ld_in + c;
+      if (VEC == 8) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      } else {
+        x[0] = src[0];
+      }
+#pragma unroll
+      for (int j = 0; j < VEC; j++) x[j] = rbf<R>(x[j]);  // gelu_row4f.cc:78-80
+    } else {
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(in) + r * ld_in + c;
+      if (VEC == 8) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          x[2 * j] = __uint_as_float(w[j] << 16);
+          x[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+        }
+      } else {
+        x[0] = bits_f32(src[0]);
+      }
+    }
+    uint16_t* dst = out + r * ld_out + c;
+    if (VEC == 8) {
+      float y[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) y[j] = gelu_poly4<R>(x[j]);
+      uint4 o;
+      o.x = pack_bf16x2<R>(y[0], y[1]);
+      o.y = pack_bf16x2<R>(y[2], y[3]);
+      o.z = pack_bf16x2<R>(y[4], y[5]);
+      o.w = pack_bf16x2<R>(y[6], y[7]);
+      *reinterpret_cast<uint4*>(dst) = o;
+    } else {
+      dst[0] = (uint16_t)bf16_bits<R>(gelu_poly4<R>(x[0]));
+    }
+  }
+}
+
+// ---------------------------------------------------------------- row helpers
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+// The 16 lane partial sums of lanes 0..15 reduced by the halving tree
+// (l, l+8) -> (l, l+4) -> (l, l+2) -> (l, l+1); every lane of the half gets it.
+__device__ __forceinline__ float lane16_tree(float acc) {
+  acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8, 16));
+  acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4, 16));
+  acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2, 16));
+  acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1, 16));
+  return acc;
+}
+
+// Stage one bf16 row window (w elements) in shared memory, optionally scaled
+// (x' = R(x * scale)), and return the row max seeded with `init`.
+template <int R>
+__device__ __forceinline__ float stage_row(const uint16_t* __restrict__ src, uint16_t* buf, int w,
+                                           bool vec, bool do_scale, float scale, float init,
+                                           bool want_max) {
+  const int lane = lane_id();
+  float m = init;
+  int done = 0;
+  if (vec) {
+    const int nv = w / 8;
+    for (int v = lane; v < nv; v += 32) {
+      uint4 q = __ldg(reinterpret_cast<const uint4*>(src) + v);
+      if (do_scale || want_max) {
+        uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          float lo = __uint_as_float(wd[j] << 16), hi = __uint_as_float(wd[j] & 0xFFFF0000u);
+          if (do_scale) {
+            lo = rbf<R>(lo * scale);
+            hi = rbf<R>(hi * scale);
+            wd[j] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
+          }
+          if (want_max) m = fmaxf(m, fmaxf(lo, hi));
+        }
+        q = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      }
+      reinterpret_cast<uint4*>(buf)[v] = q;
+    }
+    done = nv * 8;
+  }
+  for (int c = done + lane; c < w; c += 32) {
+    float x = bits_f32(src[c]);
+    if (do_scale) x = rbf<R>(x * scale);
+    buf[c] = (uint16_t)(__float_as_uint(x) >> 16);
+    if (want_max) m = fmaxf(m, x);
+  }
+  return want_max ? warp_max(m) : m;
+}
+
+// e = R(exp(R(x - max))) via the table; ea = the fp32 exponential (v3 only).
+template <int R, bool NEED32>
+__device__ __forceinline__ float exp_lookup(float x, float m, const uint16_t* t16, const float* t32,
+                                            float* ea) {
+  const float d = rbf<R>(__fsub_rn(x, m));
+  const uint32_t b = __float_as_uint(d) >> 16;
+  float e, a;
+  if (b == 0u) {
+    e = 1.0f;
+    a = 1.0f;
+  } else if (b >= (uint32_t)kExpTabBase && b < (uint32_t)(kExpTabBase + kExpTabN)) {
+    e = bits_f32(t16[b - kExpTabBase]);
+    a = NEED32 ? t32[b - kExpTabBase] : e;
+  } else {
+    e = 0.0f;
+    a = 0.0f;
+  }
+  if (NEED32) *ea = a;
+  return e;
+}
+
+// ---------------------------------------------------------------- softmax
+template <int R, int VAR>
+__global__ void __launch_bounds__(256) softmax_rows_kernel(
+    const uint16_t* __restrict__ in, uint16_t* __restrict__ out, int64_t rows, int w,
+    int64_t ld_in, int64_t ld_out, float scale, const uint16_t* __restrict__ t16_g,
+    const float* __restrict__ t32_g, int wpad, int vec_in, int vec_out) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr bool N32 = (VAR == 3);
+  uint16_t* t16 = reinterpret_cast<uint16_t*>(smem);
+  float* t32 = reinterpret_cast<float*>(smem + ((kExpTabN * 2 + 15) / 16) * 16);
+  uint8_t* rows_base = smem + ((kExpTabN * 2 + 15) / 16) * 16 + (N32 ? kExpTabN * 4 : 0);
+  for (int i = threadIdx.x; i < kExpTabN; i += blockDim.x) {
+    t16[i] = t16_g[i];
+    if (N32) t32[i] = t32_g[i];
+  }
+  __syncthreads();
+  const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
+  uint16_t* buf = reinterpret_cast<uint16_t*>(rows_base) + (size_t)warp * wpad;
+  const bool do_scale = scale != 1.0f;
+  for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
+       row += (int64_t)gridDim.x * warps) {
+    // pass 1: stage the window, row max seeded with (bfloat16)-30000 (body.inc:22-28)
+    const float m = stage_row<R>(in + row * ld_in, buf, w, vec_in, do_scale, scale, -29952.0f, true);
+    __syncwarp();
+    // pass 2: 16 fp32 lanes, lane l summing e over columns l, l+16, ... (body.inc:31-40)
+    float acc = 0.0f;
+    if (lane < 16) {
+      for (int c = lane; c < w; c += 16) {
+        float ea;
+        const float e = exp_lookup<R, false>(bits_f32(buf[c]), m, t16, t32, &ea);
+        acc = __fadd_rn(acc, e);
+      }
+    }
+    const float sum = __shfl_sync(0xffffffffu, lane16_tree(acc), 0);
+    const float inv = __fdiv_rn(1.0f, sum);                 // aie::inv
+    const float ihi = rbf<R>(inv);                          // body.inc:45-46
+    const float ilo = rbf<R>(__fsub_rn(inv, ihi));
+    // pass 3: p = R(e*hi + e*lo) (body.inc:51-60), or the v1 / v3 forms
+    auto prob = [&](float x) -> float {
+      float ea;
+      const float e = exp_lookup<R, N32>(x, m, t16, t32, &ea);
+      if (VAR == 1) return rbf<R>(__fmul_rn(e, ihi));       // softmax_row.cc:50-57
+      if (VAR == 3) {                                       // softmax_row3.cc:76-84
+        const float ehi = rbf<R>(ea);
+        const float elo = rbf<R>(__fsub_rn(ea, ehi));
+        float p = __fmul_rn(ehi, ihi);
+        p = __fadd_rn(p, __fmul_rn(ehi, ilo));
+        p = __fadd_rn(p, __fmul_rn(elo, ihi));
+        return rbf<R>(p);
+      }
+      return rbf<R>(__fadd_rn(__fmul_rn(e, ihi), __fmul_rn(e, ilo)));
+    };
+    uint16_t* dst = out + row * ld_out;
+    int done = 0;
+    if (vec_out) {
+      const int nv = w / 8;
+      for (int v = lane; v < nv; v += 32) {
+        const uint4 q = reinterpret_cast<const uint4*>(buf)[v];
+        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          o[j] = pack_bf16x2<R>(prob(__uint_as_float(wd[j] << 16)),
+                                prob(__uint_as_float(wd[j] & 0xFFFF0000u)));
+        reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      done = nv * 8;
+    }
+    for (int c = done + lane; c < w; c += 32) dst[c] = (uint16_t)bf16_bits<R>(prob(bits_f32(buf[c])));
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// kernels/layer_norm_gb.cc:22-34, every fp32 operation rounded on its own.
+__device__ __forceinline__ float rsqrt_nr(float x) {
+  float y = __uint_as_float(0x5f3759dfu - (__float_as_uint(x) >> 1));
+#pragma unroll
+  for (int i = 0; i < 3; i++) {
+    const float t = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, x), y), y);
+    y = __fmul_rn(y, __fsub_rn(1.5f, t));
+  }
+  return y;
+}
+
+template <int R>
+__global__ void __launch_bounds__(256) layernorm_aie_kernel(
+    const uint16_t* __restrict__ in, const float* __restrict__ gamma,
+    const float* __restrict__ beta, uint16_t* __restrict__ out, int64_t rows, int w,
+    int64_t ld_in, int64_t ld_out, float eps, int wpad, int vec_in, int vec_out) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
+  uint16_t* buf = reinterpret_cast<uint16_t*>(smem) + (size_t)warp * wpad;
+  const bool affine = gamma != nullptr || beta != nullptr;
+  for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
+       row += (int64_t)gridDim.x * warps) {
+    stage_row<R>(in + row * ld_in, buf, w, vec_in, false, 1.0f, 0.0f, false);
+    __syncwarp();
+    // pass 1 (:61-67): sum and sum of squares in 16 fp32 lanes
+    float s1 = 0.0f, s2 = 0.0f;
+    if (lane < 16) {
+      for (int c = lane; c < w; c += 16) {
+        const float x = bits_f32(buf[c]);
+        s1 = __fadd_rn(s1, x);
+        s2 = __fadd_rn(s2, __fmul_rn(x, x));
+      }
+    }
+    s1 = __shfl_sync(0xffffffffu, lane16_tree(s1), 0);
+    s2 = __shfl_sync(0xffffffffu, lane16_tree(s2), 0);
+    const float inv_n = __fdiv_rn(1.0f, (float)w);                       // :69
+    const float mean = __fmul_rn(s1, inv_n);                             // :70
+    const float var = __fsub_rn(__fmul_rn(s2, inv_n), __fmul_rn(mean, mean));  // :71
+    const float inv = rsqrt_nr(__fadd_rn(var, eps));                     // :72
+    const float mb = rbf<R>(mean), ib = rbf<R>(inv);                     // :74-77
+    auto norm = [&](float x, int c) -> float {                           // :80-85
+      float o = rbf<R>(__fmul_rn(rbf<R>(__fsub_rn(x, mb)), ib));
+      if (affine) {
+        const float g = gamma ? gamma[c] : 1.0f, b = beta ? beta[c] : 0.0f;
+        o = rbf<R>(__fadd_rn(__fmul_rn(o, g), b));
+      }
+      return o;
+    };
+    uint16_t* dst = out + row * ld_out;
+    int done = 0;
+    if (vec_out) {
+      const int nv = w / 8;
+      for (int v = lane; v < nv; v += 32) {
+        const uint4 q = reinterpret_cast<const uint4*>(buf)[v];
+        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          o[j] = pack_bf16x2<R>(norm(__uint_as_float(wd[j] << 16), v * 8 + 2 * j),
+                                norm(__uint_as_float(wd[j] & 0xFFFF0000u), v * 8 + 2 * j + 1));
+        reinterpret_cast<uint4*>(dst)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      done = nv * 8;
+    }
+    for (int c = done + lane; c < w; c += 32) dst[c] = (uint16_t)bf16_bits<R>(norm(bits_f32(buf[c]), c));
+    __syncwarp();
+  }
+}
+
+// fp32 two-pass LayerNorm, one warp per row; the row is kept in registers for
+// widths up to 2048 (NV = 16 float4 per lane), re-read from L2 beyond that.
+template <bool IN_BF16, bool OUT_BF16>
+__global__ void __launch_bounds__(256) layernorm_fp32_kernel(
+    const void* __restrict__ in, const float* __restrict__ gamma,
+    const float* __restrict__ beta, void* __restrict__ out, int64_t rows, int w, int64_t ld_in,
+    int64_t ld_out, float eps) {
+  constexpr int NV = 16;
+  const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
+  auto load4 = [&](int64_t row, int c) -> float4 {
+    if (IN_BF16) {
+      const uint2 q = __ldg(reinterpret_cast<const uint2*>(
+          reinterpret_cast<const uint16_t*>(in) + row * ld_in + c));
+      return make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xFFFF0000u),
+                         __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xFFFF0000u));
+    }
+    return __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in) +
+                                                 row * ld_in + c));
+  };
+  for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
+       row += (int64_t)gridDim.x * warps) {
+    float4 v[NV];
+    float s = 0.0f;
+    const bool fits = w <= NV * 128;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const int c = (i * 32 + lane) * 4;
+      if (fits && c < w) {
+        v[i] = load4(row, c);
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+      } else {
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if (!fits)
+      for (int c = lane * 4; c < w; c += 128) {
+        const float4 t = load4(row, c);
+        s += (t.x + t.y) + (t.z + t.w);
+      }
+    const float mean = warp_sum(s) / (float)w;
+    float q = 0.0f;
+    if (fits) {
+#pragma unroll
+      for (int i = 0; i < NV; i++) {
+        const int c = (i * 32 + lane) * 4;
+        if (c < w) {
+          const float a = v[i].x - mean, b = v[i].y - mean, d = v[i].z - mean, e = v[i].w - mean;
+          q += (a * a + b * b) + (d * d + e * e);
+        }
+      }
+    } else {
+      for (int c = lane * 4; c < w; c += 128) {
+        const float4 t = load4(row, c);
+        const float a = t.x - mean, b = t.y - mean, d = t.z - mean, e = t.w - mean;
+        q += (a * a + b * b) + (d * d + e * e);
+      }
+    }
+    const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)w + eps);
+    auto emit = [&](int c, float4 t) {
+      const float4 g = gamma ? __ldg(reinterpret_cast<const float4*>(gamma + c))
+                             : make_float4(1.f, 1.f, 1.f, 1.f);
+      const float4 b = beta ? __ldg(reinterpret_cast<const float4*>(beta + c))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float y0 = (t.x - mean) * rstd * g.x + b.x, y1 = (t.y - mean) * rstd * g.y + b.y;
+      const float y2 = (t.z - mean) * rstd * g.z + b.z, y3 = (t.w - mean) * rstd * g.w + b.w;
+      if (OUT_BF16) {
+        uint2 o;
+        o.x = pack_bf16x2_rne(y0, y1);
+        o.y = pack_bf16x2_rne(y2, y3);
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + row * ld_out + c) = o;
+      } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + row * ld_out + c) =
+            make_float4(y0, y1, y2, y3);
+      }
+    };
+    if (fits) {
+#pragma unroll
+      for (int i = 0; i < NV; i++) {
+        const int c = (i * 32 + lane) * 4;
+        if (c < w) emit(c, v[i]);
+      }
+    } else {
+      for (int c = lane * 4; c < w; c += 128) emit(c, load4(row, c));
+    }
+  }
+}
+
+static int grid_for(int64_t work_items, int per_block, int blocks_per_sm) {
+  int64_t g = (work_items + per_block - 1) / per_block;
+  const int64_t cap = (int64_t)sm_count() * blocks_per_sm;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int launch_gelu_poly4(const void* in, int in_dtype, void* out, int64_t rows, int64_t cols,
+                      int64_t ld_in, int64_t ld_out, int rounding, cudaStream_t st) {
+  if (rows < 0 || cols < 0) return fail(WX_ERR_INVALID, "gelu: negative shape");
+  if (rows == 0 || cols == 0) return WX_OK;
+  if (!in || !out) return fail(WX_ERR_INVALID, "gelu: NULL pointer");
+  if (ld_in < cols || ld_out < cols) return fail(WX_ERR_INVALID, "gelu: row stride < cols");
+  if (rounding != RND_TRUNC && rounding != RND_RNE)
+    return fail(WX_ERR_INVALID, "gelu: rounding %d", rounding);
+  if (in_dtype != WX_DTYPE_BF16 && in_dtype != WX_DTYPE_F32)
+    return fail(WX_ERR_INVALID, "gelu: in_dtype %d", in_dtype);
+  const bool f32 = in_dtype == WX_DTYPE_F32;
+  const bool vec = cols % 8 == 0 && ld_in % 8 == 0 && ld_out % 8 == 0 && aligned16(in) &&
+                   aligned16(out);
+  const int64_t items = rows * (vec ? cols / 8 : cols);
+  const int grid = grid_for(items, 256, 8);
+  uint16_t* o = reinterpret_cast<uint16_t*>(out);
+#define WX_GELU_LAUNCH(R, F, V) \
+  gelu_poly4_kernel<R, F, V><<<grid, 256, 0, st>>>(in, o, rows, cols, ld_in, ld_out)
+  if (rounding == RND_RNE) {
+    if (f32) { if (vec) WX_GELU_LAUNCH(RND_RNE, true, 8); else WX_GELU_LAUNCH(RND_RNE, true, 1); }
+    else { if (vec) WX_GELU_LAUNCH(RND_RNE, false, 8); else WX_GELU_LAUNCH(RND_RNE, false, 1); }
+  } else {
+    if (f32) { if (vec) WX_GELU_LAUNCH(RND_TRUNC, true, 8); else WX_GELU_LAUNCH(RND_TRUNC, true, 1); }
+    else { if (vec) WX_GELU_LAUNCH(RND_TRUNC, false, 8); else WX_GELU_LAUNCH(RND_TRUNC, false, 1); }
+  }
+#undef WX_GELU_LAUNCH
+  return check_launch("gelu_poly4");
+}
+
+// Warps per block for the row kernels: as many as the shared memory allows, up
+// to 8.
+static int row_warps(size_t fixed_bytes, size_t per_warp_bytes) {
+  const size_t budget = 200 * 1024;
+  int wps = 8;
+  while (wps > 1 && fixed_bytes + wps * per_warp_bytes > budget) wps--;
+  return wps;
+}
+
+int launch_softmax_rows(const void* in, void* out, int64_t rows, int64_t cols, int64_t valid,
+                        int64_t ld_in, int64_t ld_out, float scale, int variant, int rounding,
+                        cudaStream_t st) {
+  if (rows < 0 || cols < 0) return fail(WX_ERR_INVALID, "softmax: negative shape");
+  const int64_t w = valid > 0 ? valid : cols;
+  if (w > cols) return fail(WX_ERR_INVALID, "softmax: window %lld > cols %lld", (long long)w, (long long)cols);
+  if (rows == 0 || w == 0) return WX_OK;
+  if (w > 65536) return fail(WX_ERR_UNSUPPORTED, "softmax: window %lld > 65536", (long long)w);
+  if (!in || !out) return fail(WX_ERR_INVALID, "softmax: NULL pointer");
+  if (ld_in < w || ld_out < w) return fail(WX_ERR_INVALID, "softmax: row stride < window");
+  if (variant != 1 && variant != 3 && variant != 4)
+    return fail(WX_ERR_INVALID, "softmax: variant %d (1, 3 or 4)", variant);
+  if (rounding != RND_TRUNC && rounding != RND_RNE)
+    return fail(WX_ERR_INVALID, "softmax: rounding %d", rounding);
+  ExpTablesDev* tabs = nullptr;
+  WX_TRY(exp_tables(&tabs));
+  const int wpad = (int)((w + 7) / 8 * 8);
+  const size_t fixed = ((kExpTabN * 2 + 15) / 16) * 16 + (variant == 3 ? kExpTabN * 4 : 0);
+  const int wps = row_warps(fixed, (size_t)wpad * 2);
+  const size_t smem = fixed + (size_t)wps * wpad * 2;
+  const int vin = (w % 8 == 0 && ld_in % 8 == 0 && aligned16(in)) ? 1 : 0;
+  const int vout = (w % 8 == 0 && ld_out % 8 == 0 && aligned16(out)) ? 1 : 0;
+  const int grid = grid_for(rows, wps, 2);
+  const uint16_t* i16 = reinterpret_cast<const uint16_t*>(in);
+  uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+#define WX_SM_LAUNCH(R, V)                                                                   \
+  do {                                                                                       \
+    auto k = softmax_rows_kernel<R, V>;                                                      \
+    WX_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+    k<<<grid, wps * 32, smem, st>>>(i16, o16, rows, (int)w, ld_in, ld_out, scale,           \
+                                    tabs->t16[R], tabs->t32, wpad, vin, vout);               \
+  } while (0)
+  if (rounding == RND_RNE) {
+    if (variant == 4) WX_SM_LAUNCH(RND_RNE, 4); else if (variant == 1) WX_SM_LAUNCH(RND_RNE, 1); else WX_SM_LAUNCH(RND_RNE, 3);
+  } else {
+    if (variant == 4) WX_SM_LAUNCH(RND_TRUNC, 4); else if (variant == 1) WX_SM_LAUNCH(RND_TRUNC, 1); else WX_SM_LAUNCH(RND_TRUNC, 3);
+  }
+#undef WX_SM_LAUNCH
+  return check_launch("softmax_rows");
+}
+
+int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, const float* beta,
+                          void* out, int out_dtype, int64_t rows, int64_t cols, int64_t ld_in,
+                          int64_t ld_out, float eps, int mode, int rounding, cudaStream_t st) {
+  if (rows < 0 || cols < 0) return fail(WX_ERR_INVALID, "layernorm: negative shape");
+  if (rows == 0 || cols == 0) return WX_OK;
+  if (!in || !out) return fail(WX_ERR_INVALID, "layernorm: NULL pointer");
+  if (ld_in < cols || ld_out < cols) return fail(WX_ERR_INVALID, "layernorm: row stride < cols");
+  if (mode == WX_LN_AIE) {
+    if (in_dtype != WX_DTYPE_BF16 || out_dtype != WX_DTYPE_BF16)
+      return fail(WX_ERR_INVALID, "layernorm: WX_LN_AIE is bf16 in and out");
+    if (rounding != RND_TRUNC && rounding != RND_RNE)
+      return fail(WX_ERR_INVALID, "layernorm: rounding %d", rounding);
+    if (cols > 65536) return fail(WX_ERR_UNSUPPORTED, "layernorm: cols %lld > 65536", (long long)cols);
+    const int wpad = (int)((cols + 7) / 8 * 8);
+    const int wps = row_warps(0, (size_t)wpad * 2);
+    const size_t smem = (size_t)wps * wpad * 2;
+    const int vin = (cols % 8 == 0 && ld_in % 8 == 0 && aligned16(in)) ? 1 : 0;
+    const int vout = (cols % 8 == 0 && ld_out % 8 == 0 && aligned16(out)) ? 1 : 0;
+    const int grid = grid_for(rows, wps, 2);
+    const uint16_t* i16 = reinterpret_cast<const uint16_t*>(in);
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+    if (rounding == RND_RNE) {
+      auto k = layernorm_aie_kernel<RND_RNE>;
+      WX_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      k<<<grid, wps * 32, smem, st>>>(i16, gamma, beta, o16, rows, (int)cols, ld_in, ld_out, eps, wpad, vin, vout);
+    } else {
+      auto k = layernorm_aie_kernel<RND_TRUNC>;
+      WX_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      k<<<grid, wps * 32, smem, st>>>(i16, gamma, beta, o16, rows, (int)cols, ld_in, ld_out, eps, wpad, vin, vout);
+    }
+    return check_launch("layernorm_aie");
+  }
+  if (mode != WX_LN_FP32) return fail(WX_ERR_INVALID, "layernorm: mode %d", mode);
+  if (cols % 4 != 0 || ld_in % 4 != 0 || ld_out % 4 != 0 || !aligned16(in) || !aligned16(out) ||
+      (gamma && !aligned16(gamma)) || (beta && !aligned16(beta)))
+    return fail(WX_ERR_INVALID, "layernorm fp32: cols and strides must be multiples of 4, "
+                "pointers 16-byte aligned");
+  const int grid = grid_for(rows, 8, 4);
+  const bool ib = in_dtype == WX_DTYPE_BF16, ob = out_dtype == WX_DTYPE_BF16;
+  if (ib && ob) layernorm_fp32_kernel<true, true><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, (int)cols, ld_in, ld_out, eps);
+  else if (ib) layernorm_fp32_kernel<true, false><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, (int)cols, ld_in, ld_out, eps);
+  else if (ob) layernorm_fp32_kernel<false, true><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, (int)cols, ld_in, ld_out, eps);
+  else layernorm_fp32_kernel<false, false><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, (int)cols, ld_in, ld_out, eps);
+  return check_launch("layernorm_fp32");
+}
+
+}  // namespace wx
+
+extern "C" {
+
+int wx_gelu_poly4(const void* in, int in_dtype, void* out, int64_t rows, int64_t cols,
+                  int64_t ld_in, int64_t ld_out, int rounding, void* stream) {
+  return wx::launch_gelu_poly4(in, in_dtype, out, rows, cols, ld_in, ld_out, rounding,
+                               wx::as_stream(stream));
+}
+
+int wx_softmax_rows(const void* in, void* out, int64_t rows, int64_t cols, int64_t valid,
+                    int64_t ld_in, int64_t ld_out, float scale, int variant, int rounding,
+                    void* stream) {
+  return wx::launch_softmax_rows(in, out, rows, cols, valid, ld_in, ld_out, scale, variant,
+                                 rounding, wx::as_stream(stream));
+}
+
+int wx_layernorm_rows(const void* in, int in_dtype, const float* gamma, const float* beta,
+                      void* out, int out_dtype, int64_t rows, int64_t cols, int64_t ld_in,
+                      int64_t ld_out, float eps, int mode, int rounding, void* stream) {
+  return wx::launch_layernorm_rows(in, in_dtype, gamma, beta, out, out_dtype, rows, cols, ld_in,
+                                   ld_out, eps, mode, rounding, wx::as_stream(stream));
+}
+
+int wx_softmax_exp_table(int rounding, uint16_t* out16, float* out32, int64_t n) {
+  if (n < wx::kExpTabN) return wx::fail(WX_ERR_INVALID, "exp table needs %d entries", wx::kExpTabN);
+  std::vector<uint16_t> a(wx::kExpTabN), b(wx::kExpTabN);
+  std::vector<float> c(wx::kExpTabN);
+  wx::host_exp_tables(a.data(), b.data(), c.data());
+  for (int i = 0; i < wx::kExpTabN; i++) {
+    if (out16) out16[i] = rounding == WX_ROUND_RNE ? b[i] : a[i];
+    if (out32) out32[i] = c[i];
+  }
+  return wx::kExpTabN;
+}
+
+int wx_gelu4_table(int rounding, float* out, int64_t n) {
+  if (n < 24) return wx::fail(WX_ERR_INVALID, "gelu table needs 24 floats");
+  // The constants the kernels compile in (common.cuh), checked against the
+  // decimal literals of the reference's table rounded in `rounding`.
+  const wx::Gelu4Table t = wx::gelu4_table(rounding);
+  const float kc[3][5] = WX_GELU4_COEF;
+  const float brk[3] = {1.0f, 2.0f, 4.0f}, sh[3] = {0.5f, 1.5f, 3.0f}, sc[3] = {2.0f, 2.0f, 1.0f};
+  for (int p = 0; p < 3; p++) {
+    if (t.brk[p] != brk[p] || t.shift[p] != sh[p] || t.scale[p] != sc[p])
+      return wx::fail(WX_ERR_INVALID, "gelu table: compiled piece bounds differ");
+    for (int k = 0; k < 5; k++)
+      if (t.c[p][k] != kc[p][k])
+        return wx::fail(WX_ERR_INVALID, "gelu table: compiled coefficient %d,%d differs", p, k);
+  }
+  memcpy(out, brk, sizeof(brk));
+  memcpy(out + 3, sh, sizeof(sh));
+  memcpy(out + 6, sc, sizeof(sc));
+  memcpy(out + 9, kc, sizeof(kc));
+  return 24;
+}
+
+}  // extern "C"

@@ -1,0 +1,52 @@
+// Internal host-side helpers shared by the .cu files of libwxb200.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/wxb200.h"
+
+namespace wx {
+
+// Record the calling thread's last error; returns `code` so call sites can
+// `return fail(WX_ERR_INVALID, "...")`.
+int fail(int code, const char* fmt, ...);
+
+// Check a CUDA runtime status; on error record it and return WX_ERR_CUDA.
+#define WX_CUDA_TRY(expr)                                                            \
+  do {                                                                               \
+    cudaError_t e_ = (expr);                                                         \
+    if (e_ != cudaSuccess)                                                           \
+      return ::wx::fail(WX_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,                 \
+                        cudaGetErrorString(e_), __FILE__, __LINE__);                 \
+  } while (0)
+
+#define WX_TRY(expr)         \
+  do {                       \
+    int s_ = (expr);         \
+    if (s_ != WX_OK) return s_; \
+  } while (0)
+
+// After a kernel launch.
+int check_launch(const char* what);
+
+// The device error word kernels write into (one int per device).
+int* device_error_word();
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library does not link libcuda and loads on machines without a GPU.
+int encode_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                         int elem_bytes, uint64_t inner, uint64_t outer,
+                         uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle);
+
+// Number of SMs of the current device.
+int sm_count();
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace wx

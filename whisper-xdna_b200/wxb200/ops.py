@@ -1,0 +1,136 @@
+"""Device-tensor wrappers of the C ABI: torch CUDA tensors in and out, work
+enqueued on torch's current stream.
+
+Every function takes 2-D tensors whose last dimension is contiguous (row
+stride = tensor.stride(0)), so column bands and column slices of wider
+buffers are accepted as they are -- the banded outputs of src/rowops.py:80-88
+and the per-head slices of a fused QKV buffer.
+"""
+import ctypes
+
+import torch
+
+from . import _lib as L
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _mat(t, name, dtypes):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be 2-D with a contiguous last dimension")
+    if t.dtype not in dtypes:
+        raise ValueError(f"{name} dtype {t.dtype} not in {dtypes}")
+    return t
+
+
+def _vec(t, n, name):
+    if t is None:
+        return None
+    if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.float32:
+        raise ValueError(f"{name} must be a float32 CUDA tensor")
+    t = t.contiguous()
+    if t.numel() != n:
+        raise ValueError(f"{name} has {t.numel()} elements, expected {n}")
+    return t
+
+
+def gelu_poly4(x, out=None, rounding=L.WX_ROUND_RNE):
+    """GELU-poly4 of a bf16 (g4 / g4r) or fp32 (g4f) matrix into bf16 `out`."""
+    _mat(x, "x", (torch.bfloat16, torch.float32))
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty(rows, cols, dtype=torch.bfloat16, device=x.device)
+    _mat(out, "out", (torch.bfloat16,))
+    if tuple(out.shape) != (rows, cols):
+        raise ValueError("out shape mismatch")
+    dt = L.WX_DTYPE_F32 if x.dtype == torch.float32 else L.WX_DTYPE_BF16
+    L.check(L.lib().wx_gelu_poly4(_ptr(x), dt, _ptr(out), rows, cols, x.stride(0),
+                                  out.stride(0), rounding, _stream()))
+    return out
+
+
+def softmax_rows(x, out=None, valid=0, scale=1.0, variant=4, rounding=L.WX_ROUND_TRUNC):
+    """Row softmax over the first `valid` columns (all if 0) of bf16 rows."""
+    _mat(x, "x", (torch.bfloat16,))
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty(rows, cols, dtype=torch.bfloat16, device=x.device)
+    _mat(out, "out", (torch.bfloat16,))
+    if out.shape[0] != rows or out.shape[1] < (valid if valid > 0 else cols):
+        raise ValueError("out shape mismatch")
+    L.check(L.lib().wx_softmax_rows(_ptr(x), _ptr(out), rows, cols, valid, x.stride(0),
+                                    out.stride(0), float(scale), variant, rounding, _stream()))
+    return out
+
+
+def layer_norm_rows(x, gamma=None, beta=None, out=None, eps=1e-5, mode=L.WX_LN_AIE,
+                    rounding=L.WX_ROUND_TRUNC, out_dtype=None):
+    """LayerNorm of each row (mode WX_LN_AIE: the reference's device kernel,
+    bf16; WX_LN_FP32: fp32 two-pass, bf16 or fp32 in and out)."""
+    _mat(x, "x", (torch.bfloat16, torch.float32))
+    rows, cols = x.shape
+    if out is None:
+        od = out_dtype or (torch.bfloat16 if mode == L.WX_LN_AIE else x.dtype)
+        out = torch.empty(rows, cols, dtype=od, device=x.device)
+    _mat(out, "out", (torch.bfloat16, torch.float32))
+    g, b = _vec(gamma, cols, "gamma"), _vec(beta, cols, "beta")
+    idt = L.WX_DTYPE_F32 if x.dtype == torch.float32 else L.WX_DTYPE_BF16
+    odt = L.WX_DTYPE_F32 if out.dtype == torch.float32 else L.WX_DTYPE_BF16
+    L.check(L.lib().wx_layernorm_rows(_ptr(x), idt, _ptr(g), _ptr(b), _ptr(out), odt, rows,
+                                      cols, x.stride(0), out.stride(0), float(eps), mode,
+                                      rounding, _stream()))
+    return out
+
+
+def gemm(A, W, bias=None, residual=None, out=None, epilogue=None):
+    """epilogue(A @ W^T) on the tensor cores: A (M, K) bf16, W (N, K) bf16.
+
+    Default epilogue: fp32 output (+ residual when given)."""
+    _mat(A, "A", (torch.bfloat16,))
+    _mat(W, "W", (torch.bfloat16,))
+    M, K = A.shape
+    N, K2 = W.shape
+    if K != K2:
+        raise ValueError(f"inner dimensions differ: {K} vs {K2}")
+    if epilogue is None:
+        epilogue = L.WX_EPI_F32_RESID if residual is not None else L.WX_EPI_F32
+    f32_out = epilogue in (L.WX_EPI_F32, L.WX_EPI_F32_RESID)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32 if f32_out else torch.bfloat16,
+                          device=A.device)
+    _mat(out, "out", (torch.float32,) if f32_out else (torch.bfloat16,))
+    b = _vec(bias, N, "bias")
+    r = None
+    if residual is not None:
+        r = _mat(residual, "residual", (torch.float32,))
+    L.check(L.lib().wx_gemm_bf16(_ptr(A), _ptr(W), _ptr(b), _ptr(r), _ptr(out), M, N, K,
+                                 A.stride(0), W.stride(0), out.stride(0),
+                                 r.stride(0) if r is not None else 0, epilogue, _stream()))
+    return out
+
+
+def attention(q, k, v, n_batch, n_head, scale, out=None):
+    """softmax(scale * q k^T) v per (batch, head); q, k, v: (n_batch*T, n_head*64)
+    bf16 (column slices of one QKV buffer are fine)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _mat(t, n, (torch.bfloat16,))
+    rows, width = q.shape
+    if rows % n_batch:
+        raise ValueError("rows not divisible by n_batch")
+    T = rows // n_batch
+    hd = width // n_head
+    if out is None:
+        out = torch.empty(rows, width, dtype=torch.bfloat16, device=q.device)
+    _mat(out, "out", (torch.bfloat16,))
+    L.check(L.lib().wx_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(out), n_batch, n_head, T, hd,
+                                 q.stride(0), k.stride(0), v.stride(0), out.stride(0),
+                                 float(scale), _stream()))
+    return out
