@@ -3,20 +3,26 @@
 // QK -> softmax -> AV chain of the reference in one kernel, with the scores
 // never leaving the SM.
 //
-// One CTA per (128-query tile, head, clip); 6 warps:
-//   warp 0     TMA: the Q tile once, then K and V tiles (128 keys x 64) into
-//              two-slot rings (separate K and V barriers, so a K slot frees as
-//              soon as its QK^T is done)
-//   warp 1     allocates tensor memory, issues S = Q K^T (M=128, N=128, K=64)
-//              into one of two S buffers and O_j = P_j V_j (M=128, N=64, K=128,
-//              V read MN-major straight from its row-major tile) into one of
-//              two O buffers
-//   warps 2-5  online softmax, one query row per thread: tcgen05.ld of the S
-//              row, running max in the exp2 domain, P = exp2(s*c - m) written
-//              as bf16 into shared memory in the 128-byte-swizzled K-major
-//              layout the PV MMA reads, and the fp32 output row kept in
-//              registers: O = O * exp2(m_old - m_new) + P_j V_j, divided by the
-//              row sum at the end.
+// One CTA per (pair of 128-query tiles A and B, head, clip); 10 warps:
+//   warp 0     TMA: the two Q tiles once, then K and V tiles (128 keys x 64)
+//              into two-slot rings with separate K and V barriers
+//   warp 1     allocates tensor memory and issues, per key block j,
+//              S_A = Q_A K_j^T, O_A += P_A V_j, S_B = Q_B K_j^T, O_B += P_B V_j
+//              (M=128; S: N=128, K=64; PV: N=64, K=128 with V read MN-major
+//              straight from its row-major tile), O accumulating in tensor
+//              memory across blocks
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B, one query row per
+//              thread: the S row is loaded from tensor memory once and the
+//              buffer released at once, so the next QK^T overlaps this block's
+//              exponentials; P = exp2(s*c - m) goes to shared memory as bf16 in
+//              the 128-byte-swizzled K-major layout the PV MMA reads.
+// The two tiles' softmax warpgroups alternate with each other's MMAs.
+//
+// Online softmax with lazy rescaling: the running max m only moves when a
+// block's row max exceeds it by more than 8 (in log2 units); then O (read and
+// written back in tensor memory) and the row sum l are scaled by
+// exp2(m_old - m_new). Otherwise P is taken against the stale max, which keeps
+// every p <= 2^8 -- exact in the final O / l because O and l share the max.
 // The recurrence is the one of the reference's fused head kernel
 // (kernels/attn_fused.cc:13-17, src/attn_fused.py): m' = max(m, rowmax S),
 // c = exp(m - m'), l' = c l + rowsum exp(S - m'), O' = c O + exp(S - m') V.
@@ -27,46 +33,65 @@
 
 namespace wx {
 
-constexpr int kAttBQ = 128;
-constexpr int kAttBK = 128;
+constexpr int kAttBQ = 128;                       // rows per Q tile (2 tiles per CTA)
+constexpr int kAttBK = 128;                       // keys per block
 constexpr int kAttHD = 64;
-constexpr int kTileBytes = 128 * kAttHD * 2;     // 16 KB: Q, K or V tile
-constexpr int kPBytes = kAttBQ * kAttBK * 2;     // 32 KB: P tile
-constexpr int kAttSmem = 1024 + kTileBytes * 5 + kPBytes * 2 + 512;
-constexpr int kAttTmemCols = 512;                // S: 2 x 128, O: 2 x 64
-constexpr int kSCol = 0;
-constexpr int kOCol = 256;
+constexpr int kAttThreads = 320;
+constexpr int kTileBytes = 128 * kAttHD * 2;      // 16 KB: Q, K or V tile
+constexpr int kPBytes = kAttBQ * kAttBK * 2;      // 32 KB: P tile
+// Q_A, Q_B, K x2, V x2, P_A, P_B
+constexpr int kAttSmem = 1024 + kTileBytes * 6 + kPBytes * 2 + 512;
+constexpr int kAttTmemCols = 512;
+constexpr int kSCol = 0;      // S_A at 0, S_B at 128
+constexpr int kOCol = 256;    // O_A at 256, O_B at 320
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 10 warps: three share a sub-partition's 16K registers, so at most 168 each.
+__global__ void __launch_bounds__(kAttThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + kTileBytes;            // 2 slots
-  uint8_t* sV = smem + 3 * kTileBytes;        // 2 slots
-  uint8_t* sP = smem + 5 * kTileBytes;        // 2 slots of 32 KB
+  uint8_t* sQ = smem;                          // 2 tiles
+  uint8_t* sK = smem + 2 * kTileBytes;         // 2 slots
+  uint8_t* sV = smem + 4 * kTileBytes;         // 2 slots
+  uint8_t* sP = smem + 6 * kTileBytes;         // 2 tiles of 32 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;  // [2]
-  uint64_t* p_empty = bars + 15; // [2]
-  uint64_t* o_full = bars + 17;  // [2]
-  uint64_t* o_empty = bars + 19; // [2]
-  uint64_t* done = bars + 21;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  uint64_t* k_full = bars + 1;    // [2] per slot
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2] per tile
+  uint64_t* s_empty = bars + 11;  // [2]
+  uint64_t* p_full = bars + 13;   // [2]
+  uint64_t* o_done = bars + 15;   // [2]
+  uint64_t* done = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
   const int warp = warp_id(), lane = lane_id();
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int h = blockIdx.y, b = blockIdx.z;
   const int T = a.T;
-  const int q0 = qt * kAttBQ;
+  const int q0 = blockIdx.x * 2 * kAttBQ;
   const int row0 = b * T;
   const int nkv = (T + kAttBK - 1) / kAttBK;
 
@@ -80,9 +105,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
       mbar_init(&p_full[i], 128);
-      mbar_init(&p_empty[i], 1);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
+      mbar_init(&o_done[i], 1);
     }
     mbar_init(done, 1);
     fence_mbar_init();
@@ -102,10 +125,11 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      mbar_arrive_expect_tx(q_full, kTileBytes);
+      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
       tma_load_2d(&tmQ, q_full, sQ, h * kAttHD, row0 + q0);
+      tma_load_2d(&tmQ, q_full, sQ + kTileBytes, h * kAttHD, row0 + q0 + kAttBQ);
       uint32_t issued_k = 0, issued_v = 0;
-      int last_k_phase[2] = {0, 0}, last_v_phase[2] = {0, 0};
+      uint32_t last_k_phase = 0, last_v_phase = 0;
       bool ok = true;
       for (int j = 0; ok && j < nkv; j++) {
         const int s = j & 1;
@@ -114,18 +138,18 @@ __global__ void __launch_bounds__(192, 1)
         mbar_arrive_expect_tx(&k_full[s], kTileBytes);
         tma_load_2d(&tmK, &k_full[s], sK + s * kTileBytes, h * kAttHD, row0 + j * kAttBK);
         issued_k |= 1u << s;
-        last_k_phase[s] = ph;
+        last_k_phase = (last_k_phase & ~(1u << s)) | (ph << s);
         if (!mbar_wait(&v_empty[s], ph ^ 1, a.err)) { ok = false; break; }
         mbar_arrive_expect_tx(&v_full[s], kTileBytes);
         tma_load_2d(&tmV, &v_full[s], sV + s * kTileBytes, h * kAttHD, row0 + j * kAttBK);
         issued_v |= 1u << s;
-        last_v_phase[s] = ph;
+        last_v_phase = (last_v_phase & ~(1u << s)) | (ph << s);
       }
       if (!ok) {  // drain copies in flight (1 ms at most each)
         mbar_wait_for(q_full, 0, 1000000ull);
         for (int s = 0; s < 2; s++) {
-          if (issued_k & (1u << s)) mbar_wait_for(&k_full[s], last_k_phase[s], 1000000ull);
-          if (issued_v & (1u << s)) mbar_wait_for(&v_full[s], last_v_phase[s], 1000000ull);
+          if (issued_k & (1u << s)) mbar_wait_for(&k_full[s], (last_k_phase >> s) & 1u, 1000000ull);
+          if (issued_v & (1u << s)) mbar_wait_for(&v_full[s], (last_v_phase >> s) & 1u, 1000000ull);
         }
       }
     }
@@ -134,147 +158,182 @@ __global__ void __launch_bounds__(192, 1)
       // ---------------- MMA issuer
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kAttBQ, kAttBK, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(kAttBQ, kAttHD, 0, 1);
-      const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, a.err);
-      auto issue_s = [&](int j) -> bool {
+      // S_t(j) = Q_t K_j^T; the K slot frees once tile B's product is done
+      auto issue_s = [&](int t, int j) -> bool {
         const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_full[s], ph, a.err)) return false;
-        if (!mbar_wait(&s_empty[s], ph ^ 1, a.err)) return false;
+        if (t == 0 && !mbar_wait(&k_full[s], (j >> 1) & 1, a.err)) return false;
+        if (j > 0 && !mbar_wait(&s_empty[t], (j - 1) & 1, a.err)) return false;
         tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + t * kTileBytes);
         const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
-        const uint32_t d = tmem + kSCol + s * kAttBK;
+        const uint32_t d = tmem + kSCol + t * kAttBK;
 #pragma unroll
         for (int kk = 0; kk < kAttHD / 16; kk++)
           umma_bf16_ss(d, sdesc_kmajor_sw128(q_addr + kk * 32),
                        sdesc_kmajor_sw128(k_addr + kk * 32), idesc_qk, kk != 0);
-        umma_commit(&s_full[s]);
-        umma_commit(&k_empty[s]);
+        umma_commit(&s_full[t]);
+        if (t == 1) umma_commit(&k_empty[s]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < nkv; j++) {
-        if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
+      // O_t += P_t V_j; the V slot frees once tile B's product is done
+      auto issue_pv = [&](int t, int j) -> bool {
         const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&p_full[s], ph, a.err)) { ok = false; break; }
-        if (!mbar_wait(&v_full[s], ph, a.err)) { ok = false; break; }
-        if (!mbar_wait(&o_empty[s], ph ^ 1, a.err)) { ok = false; break; }
+        if (!mbar_wait(&p_full[t], j & 1, a.err)) return false;
+        if (t == 0 && !mbar_wait(&v_full[s], (j >> 1) & 1, a.err)) return false;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + s * kPBytes);
+        const uint32_t p_addr = smem_u32(sP + t * kPBytes);
         const uint32_t v_addr = smem_u32(sV + s * kTileBytes);
-        const uint32_t d = tmem + kOCol + s * kAttHD;
+        const uint32_t d = tmem + kOCol + t * kAttHD;
 #pragma unroll
         for (int kk = 0; kk < kAttBK / 16; kk++)
           umma_bf16_ss(d, sdesc_kmajor_sw128(p_addr + (kk >> 2) * (kPBytes / 2) + (kk & 3) * 32),
-                       sdesc_mnmajor_sw128(v_addr + kk * 2048, kTileBytes), idesc_pv, kk != 0);
-        umma_commit(&o_full[s]);
-        umma_commit(&v_empty[s]);
-        umma_commit(&p_empty[s]);
+                       sdesc_mnmajor_sw128(v_addr + kk * 2048, kTileBytes), idesc_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&o_done[t]);
+        if (t == 1) umma_commit(&v_empty[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
+      for (int j = 0; ok && j < nkv; j++) {
+        const bool more = j + 1 < nkv;
+        if (more && !issue_s(0, j + 1)) { ok = false; break; }
+        if (!issue_pv(0, j)) { ok = false; break; }
+        if (more && !issue_s(1, j + 1)) { ok = false; break; }
+        if (!issue_pv(1, j)) { ok = false; break; }
       }
       umma_commit(done);
       mbar_wait_for(done, 0, kWaitTimeoutNs);
     }
   } else {
-    // ---------------- softmax: warps 2..5, thread <-> query row
+    // ---------------- softmax: warps 2-5 tile A, 6-9 tile B; thread <-> row
+    const int t = (warp - 2) >> 2;
     const int sub = warp & 3;
     const int r = sub * 32 + lane;  // row within the tile
     const uint32_t t_lane = tmem + ((uint32_t)(sub * 32) << 16);
+    const uint32_t t_s = t_lane + kSCol + t * kAttBK;
+    const uint32_t t_o = t_lane + kOCol + t * kAttHD;
+    uint8_t* prow = sP + t * kPBytes + r * 128;
     const float c = a.scale_log2;
-    float m = -INFINITY, l = 0.0f, corr_prev = 0.0f;
-    float o[kAttHD];
-#pragma unroll
-    for (int i = 0; i < kAttHD; i++) o[i] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    auto fold = [&](int j, float corr) -> bool {  // O = O * corr + P_j V_j
-      const int s = j & 1;
-      if (!mbar_wait(&o_full[s], (j >> 1) & 1, a.err)) return false;
-      tc_fence_after();
-      uint32_t v0[32], v1[32];
-      tmem_ld32(t_lane + kOCol + s * kAttHD, v0);
-      tmem_ld32(t_lane + kOCol + s * kAttHD + 32, v1);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&o_empty[s]);
-#pragma unroll
-      for (int i = 0; i < 32; i++) {
-        o[i] = fmaf(o[i], corr, __uint_as_float(v0[i]));
-        o[32 + i] = fmaf(o[32 + i], corr, __uint_as_float(v1[i]));
-      }
-      return true;
-    };
     for (int j = 0; j < nkv; j++) {
-      const int s = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
       const int kvalid = min(kAttBK, T - j * kAttBK);
-      if (!mbar_wait(&s_full[s], ph, a.err)) { ok = false; break; }
+      if (!mbar_wait(&s_full[t], j & 1, a.err)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t t_s = t_lane + kSCol + s * kAttBK;
-      // pass A: row max of the valid keys
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int ch = 0; ch < kAttBK / 32; ch++) {
-        uint32_t v[32];
-        tmem_ld32(t_s + ch * 32, v);
-        tmem_wait_ld();
+      // the S row as four 32-column register arrays (separate arrays keep
+      // them in registers)
+      uint32_t s0[32], s1[32], s2[32], s3[32];
+      tmem_ld32(t_s + 0, s0);
+      tmem_ld32(t_s + 32, s1);
+      tmem_ld32(t_s + 64, s2);
+      tmem_ld32(t_s + 96, s3);
+      tmem_wait_ld();
+      // S is in registers: the next QK^T may overwrite the buffer
+      tc_fence_before();
+      mbar_arrive(&s_empty[t]);
+      // row max over the valid keys as a tree (short dependency chains)
+      auto chunk_max = [&](const uint32_t (&v)[32], int base) -> float {
+        float mm[8];
+        if (kvalid >= base + 32) {
 #pragma unroll
-        for (int i = 0; i < 32; i++)
-          if (ch * 32 + i < kvalid) mx = fmaxf(mx, __uint_as_float(v[i]));
-      }
-      const float m_new = fmaxf(m, mx * c);
-      const float corr = fast_exp2(m - m_new);
-      // P must not be overwritten while the PV MMA of two blocks ago reads it
-      if (!mbar_wait(&p_empty[s], ph ^ 1, a.err)) { ok = false; break; }
-      uint8_t* prow = sP + s * kPBytes + r * 128;
-      float sum = 0.0f;
-#pragma unroll 1
-      for (int ch = 0; ch < kAttBK / 32; ch++) {
-        uint32_t v[32];
-        tmem_ld32(t_s + ch * 32, v);
-        tmem_wait_ld();
-        uint32_t pk[16];
+          for (int i = 0; i < 8; i++)
+            mm[i] = fmaxf(fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 8])),
+                          fmaxf(__uint_as_float(v[i + 16]), __uint_as_float(v[i + 24])));
+        } else {
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const bool in0 = ch * 32 + i < kvalid, in1 = ch * 32 + i + 1 < kvalid;
-          const float p0 = in0 ? fast_exp2(fmaf(__uint_as_float(v[i]), c, -m_new)) : 0.0f;
-          const float p1 = in1 ? fast_exp2(fmaf(__uint_as_float(v[i + 1]), c, -m_new)) : 0.0f;
-          const uint32_t w = pack_bf16x2_rne(p0, p1);
-          pk[i >> 1] = w;
-          // the row sum takes the bf16 values the PV product uses
-          sum += __uint_as_float(w << 16) + __uint_as_float(w & 0xFFFF0000u);
+          for (int i = 0; i < 8; i++) {
+            mm[i] = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+              if (base + i + 8 * k < kvalid) mm[i] = fmaxf(mm[i], __uint_as_float(v[i + 8 * k]));
+          }
         }
-        // 32 keys = 4 chunks of 16 bytes; key block half = ch / 2
+        return fmaxf(fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3])),
+                     fmaxf(fmaxf(mm[4], mm[5]), fmaxf(mm[6], mm[7])));
+      };
+      float mx = fmaxf(fmaxf(chunk_max(s0, 0), chunk_max(s1, 32)),
+                       fmaxf(chunk_max(s2, 64), chunk_max(s3, 96)));
+      mx *= c;
+      const bool grow = mx > m + kRescaleThreshold;  // includes the first block
+      const float m_use = grow ? mx : m;
+      const float corr = fast_exp2(m - m_use);        // 1 when m stays, 0 on block 0
+      // P_t(j-1) V must have been consumed before P is rewritten (and before
+      // O is rescaled)
+      if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, a.err)) { ok = false; break; }
+      m = m_use;
+      float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent accumulators
+      const float negm = -m;
+      // 32 keys = 4 chunks of 8 keys (16 bytes each) of the swizzled P row
+      auto chunk_p = [&](const uint32_t (&v)[32], int base) {
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-          const int chunk = (ch & 1) * 4 + q;                  // 16-byte chunk in the row
-          uint8_t* dst = prow + (ch >> 1) * (kPBytes / 2) + ((chunk ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        }
-      }
-      // S buffer fully read; P visible to the tensor core
-      tc_fence_before();
-      mbar_arrive(&s_empty[s]);
-      fence_proxy_async_smem();
-      mbar_arrive(&p_full[s]);
-      l = l * corr + sum;
-      if (j >= 1 && !fold(j - 1, corr_prev)) { ok = false; break; }
-      corr_prev = corr;
-      m = m_new;
-    }
-    if (ok) ok = fold(nkv - 1, corr_prev);
-    if (ok && q0 + r < T) {
-      const float inv = 1.0f / l;
-      uint16_t* dst = reinterpret_cast<uint16_t*>(a.O) + (int64_t)(row0 + q0 + r) * a.ldo +
-                      h * kAttHD;
+          uint32_t w[4];
 #pragma unroll
-      for (int i = 0; i < kAttHD; i += 8) {
-        uint4 w;
-        w.x = pack_bf16x2_rne(o[i] * inv, o[i + 1] * inv);
-        w.y = pack_bf16x2_rne(o[i + 2] * inv, o[i + 3] * inv);
-        w.z = pack_bf16x2_rne(o[i + 4] * inv, o[i + 5] * inv);
-        w.w = pack_bf16x2_rne(o[i + 6] * inv, o[i + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + i) = w;
+          for (int e = 0; e < 4; e++) {
+            const int i = q * 8 + 2 * e;
+            const float p0 =
+                (base + i < kvalid) ? fast_exp2(fmaf(__uint_as_float(v[i]), c, negm)) : 0.0f;
+            const float p1 =
+                (base + i + 1 < kvalid) ? fast_exp2(fmaf(__uint_as_float(v[i + 1]), c, negm)) : 0.0f;
+            w[e] = pack_bf16x2_rne(p0, p1);
+            sums[e] += p0 + p1;
+          }
+          const int chunk = base / 8 + q;  // 16-byte chunk index along the row (0..15)
+          uint8_t* dst = prow + (chunk >> 3) * (kPBytes / 2) + (((chunk & 7) ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      };
+      chunk_p(s0, 0);
+      chunk_p(s1, 32);
+      chunk_p(s2, 64);
+      chunk_p(s3, 96);
+      // O rescale after P is written, so the S registers are free; PV(j) reads
+      // O only after p_full below
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        tc_fence_after();
+        uint32_t ov[32];
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+          tmem_ld32(t_o + half * 32, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i++) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
+          tmem_st32(t_o + half * 32, ov);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[t]);
+      l = l * corr + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
+    }
+    if (ok) ok = mbar_wait(&o_done[t], (nkv - 1) & 1, a.err);
+    if (ok) {
+      tc_fence_after();
+      uint32_t o0[32], o1[32];
+      tmem_ld32(t_o, o0);
+      tmem_ld32(t_o + 32, o1);
+      tmem_wait_ld();
+      const int qrow = q0 + t * kAttBQ + r;
+      if (qrow < T) {
+        const float inv = 1.0f / l;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(a.O) + (int64_t)(row0 + qrow) * a.ldo +
+                        h * kAttHD;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w0, w1;
+          w0.x = pack_bf16x2_rne(__uint_as_float(o0[i]) * inv, __uint_as_float(o0[i + 1]) * inv);
+          w0.y = pack_bf16x2_rne(__uint_as_float(o0[i + 2]) * inv, __uint_as_float(o0[i + 3]) * inv);
+          w0.z = pack_bf16x2_rne(__uint_as_float(o0[i + 4]) * inv, __uint_as_float(o0[i + 5]) * inv);
+          w0.w = pack_bf16x2_rne(__uint_as_float(o0[i + 6]) * inv, __uint_as_float(o0[i + 7]) * inv);
+          w1.x = pack_bf16x2_rne(__uint_as_float(o1[i]) * inv, __uint_as_float(o1[i + 1]) * inv);
+          w1.y = pack_bf16x2_rne(__uint_as_float(o1[i + 2]) * inv, __uint_as_float(o1[i + 3]) * inv);
+          w1.z = pack_bf16x2_rne(__uint_as_float(o1[i + 4]) * inv, __uint_as_float(o1[i + 5]) * inv);
+          w1.w = pack_bf16x2_rne(__uint_as_float(o1[i + 6]) * inv, __uint_as_float(o1[i + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + i) = w0;
+          *reinterpret_cast<uint4*>(dst + 32 + i) = w1;
+        }
       }
     }
   }
@@ -302,7 +361,8 @@ int attn_plan(AttnPlan* p, const void* q, const void* k, const void* v, void* o,
   int* err = device_error_word();
   if (!err) return fail(WX_ERR_CUDA, "attention: device error word unavailable");
   const uint64_t rows = (uint64_t)(B * T);
-  // Columns beyond H*hd are outside the map: a box never reaches them.
+  // Columns beyond H*hd are outside the map: a box never reaches them. Rows
+  // past B*T read as zeros.
   WX_TRY(encode_tensor_map_2d(&p->tmQ, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)need,
                               rows, (uint64_t)ldq * 2, kAttHD, kAttBQ, CU_TENSOR_MAP_SWIZZLE_128B));
   WX_TRY(encode_tensor_map_2d(&p->tmK, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)need,
@@ -312,7 +372,7 @@ int attn_plan(AttnPlan* p, const void* q, const void* k, const void* v, void* o,
   AttnArgs& g = p->args;
   g.T = (int)T;
   g.H = (int)H;
-  g.num_q_tiles = (int)((T + kAttBQ - 1) / kAttBQ);
+  g.num_q_tiles = (int)((T + 2 * kAttBQ - 1) / (2 * kAttBQ));  // tile pairs
   g.O = o;
   g.ldo = ldo;
   g.scale_log2 = scale * 1.4426950408889634f;
@@ -332,7 +392,7 @@ int attn_plan(AttnPlan* p, const void* q, const void* k, const void* v, void* o,
 
 int attn_run(const AttnPlan& p, cudaStream_t st) {
   dim3 grid(p.args.num_q_tiles, p.args.H, p.B);
-  attention_kernel<<<grid, 192, kAttSmem, st>>>(p.tmQ, p.tmK, p.tmV, p.args);
+  attention_kernel<<<grid, kAttThreads, kAttSmem, st>>>(p.tmQ, p.tmK, p.tmV, p.args);
   return check_launch("attention");
 }
 

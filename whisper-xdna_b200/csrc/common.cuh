@@ -62,27 +62,57 @@ Gelu4Table gelu4_table(int mode);
    {0x1.1ap-9f, -0x1.d6p-8f, -0x1.08p-8f, 0x1.06p-4f, -0x1.9ap-4f},                    \
    {-0x1.8p-9f, 0x1.5ep-7f, -0x1.04p-6f, 0x1.8ap-7f, -0x1.08p-8f}}
 
+// Round two fp32 values to bf16-representable values (one packed conversion
+// in RNE mode).
+template <int R>
+__device__ __forceinline__ void rbf2(float& a, float& b) {
+  if (R == RND_TRUNC) {
+    a = __uint_as_float(__float_as_uint(a) & 0xFFFF0000u);
+    b = __uint_as_float(__float_as_uint(b) & 0xFFFF0000u);
+  } else {
+    const uint32_t p = pack_bf16x2_rne(a, b);
+    a = __uint_as_float(p << 16);
+    b = __uint_as_float(p & 0xFFFF0000u);
+  }
+}
+
+// GELU-poly4 of two bf16 values (kernels/gelu_poly4_eval.inc:27-65). The
+// piece is selected, not branched on: every element runs one Horner chain
+// with the coefficients of its piece, and elements past the last break keep
+// q = 0 whatever that chain computed, so the compiler can interleave the
+// chains of many elements.
+template <int R>
+__device__ __forceinline__ void gelu_poly4_x2(float& x0, float& x1) {
+  constexpr float kC[3][5] = WX_GELU4_COEF;
+  const float s0 = fabsf(x0), s1 = fabsf(x1);    // s = max(x, 0 - x)
+  const bool a0 = s0 < 1.0f, b0 = s0 < 2.0f, in0 = s0 < 4.0f;
+  const bool a1 = s1 < 1.0f, b1 = s1 < 2.0f, in1 = s1 < 4.0f;
+  float t0 = s0 - (a0 ? 0.5f : (b0 ? 1.5f : 3.0f));
+  float t1 = s1 - (a1 ? 0.5f : (b1 ? 1.5f : 3.0f));
+  rbf2<R>(t0, t1);                                // bf16 sub
+  float u0 = t0 * (b0 ? 2.0f : 1.0f), u1 = t1 * (b1 ? 2.0f : 1.0f);
+  rbf2<R>(u0, u1);                                // bf16 mul
+  float acc0 = a0 ? kC[0][0] : (b0 ? kC[1][0] : kC[2][0]);
+  float acc1 = a1 ? kC[0][0] : (b1 ? kC[1][0] : kC[2][0]);
+#pragma unroll
+  for (int k = 1; k < 5; k++) {                   // Horner, fp32 MAC, bf16 state
+    rbf2<R>(acc0, acc1);
+    acc0 = fmaf(acc0, u0, a0 ? kC[0][k] : (b0 ? kC[1][k] : kC[2][k]));
+    acc1 = fmaf(acc1, u1, a1 ? kC[0][k] : (b1 ? kC[1][k] : kC[2][k]));
+  }
+  rbf2<R>(acc0, acc1);
+  float r0 = ((x0 >= 0.0f) ? x0 : 0.0f) + (in0 ? acc0 : 0.0f);   // relu(x) + q
+  float r1 = ((x1 >= 0.0f) ? x1 : 0.0f) + (in1 ? acc1 : 0.0f);
+  rbf2<R>(r0, r1);
+  x0 = r0;
+  x1 = r1;
+}
+
 template <int R>
 __device__ __forceinline__ float gelu_poly4(float x) {
-  constexpr float kC[3][5] = WX_GELU4_COEF;
-  // x holds a bf16 value. s = max(x, 0 - x)
-  const float s = fabsf(x);
-  const bool p0 = s < 1.0f, p1 = s < 2.0f, p2 = s < 4.0f;
-  float q = 0.0f;
-  if (p2) {  // the innermost piece with s < break wins (:40-61)
-    const float sh = p0 ? 0.5f : (p1 ? 1.5f : 3.0f);
-    const float sc = p2 && !p1 ? 1.0f : 2.0f;
-    float c[5];
-#pragma unroll
-    for (int k = 0; k < 5; k++) c[k] = p0 ? kC[0][k] : (p1 ? kC[1][k] : kC[2][k]);
-    const float u = rbf<R>(rbf<R>(s - sh) * sc);     // bf16 sub, bf16 mul
-    float acc = c[0];
-#pragma unroll
-    for (int k = 1; k < 5; k++) acc = fmaf(rbf<R>(acc), u, c[k]);  // exact product
-    q = rbf<R>(acc);
-  }
-  const float relu = (x >= 0.0f) ? x : 0.0f;          // aie::max(x, zero)
-  return rbf<R>(relu + q);
+  float y = 0.0f;
+  gelu_poly4_x2<R>(x, y);
+  return x;
 }
 
 // 2^x on the SFU (MUFU.EX2), flushing denormal results; 2^-inf = +0.

@@ -4,14 +4,15 @@
 //   C = epilogue(A @ B^T), A (M x K) bf16 row-major, B (N x K) bf16 row-major
 //   (the torch Linear weight), fp32 accumulator in tensor memory.
 //
-// Design (one persistent CTA per SM, 6 warps):
+// Design (one persistent CTA per SM, 10 warps):
 //   warp 0     TMA producer: A and B tiles (128 x 64 and BN x 64 bf16, 128-byte
 //              swizzle) into a STAGES-deep shared-memory ring
 //   warp 1     allocates tensor memory and issues tcgen05.mma (M=128, N=BN,
 //              K=16 per instruction) from one thread; tcgen05.commit frees the
 //              ring slot and publishes the finished accumulator
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
-//              32*(w%4)...), bias / residual / GELU, bf16 or fp32 stores
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//              32*(w%4)...; warps 2-5 take the first half of the columns, 6-9
+//              the second), bias / residual / GELU, bf16 or fp32 stores
 // The accumulator is double-buffered in tensor memory (2 x BN columns), so the
 // epilogue of one tile overlaps the MMAs of the next. Tiles are visited
 // N-fastest so the CTAs in flight share A tiles through L2; the weights
@@ -81,7 +82,10 @@ __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int row, int
   }
   if (EPI == WX_EPI_BF16_GELU || EPI == kEpiF32GeluPos) {
 #pragma unroll
-    for (int j = 0; j < 32; j++) v[j] = gelu_poly4<RND_RNE>(rbf<RND_RNE>(v[j]));
+    for (int j = 0; j < 32; j += 2) {  // g4f: input rounded to bf16 (RNE), then poly4
+      rbf2<RND_RNE>(v[j], v[j + 1]);
+      gelu_poly4_x2<RND_RNE>(v[j], v[j + 1]);
+    }
   }
   if (EPI == WX_EPI_BF16_GELU_ERF || EPI == kEpiF32GeluErfPos) {
 #pragma unroll
@@ -133,8 +137,11 @@ __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int row, int
   }
 }
 
+constexpr int kGemmThreads = 320;
+constexpr int kGemmEpiThreads = 256;
+
 template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
   using Cfg = GemmCfg<BN>;
@@ -160,7 +167,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], kGemmEpiThreads);
     }
     mbar_init(done, 1);
     fence_mbar_init();
@@ -235,8 +242,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait_for(done, 0, kWaitTimeoutNs);
     }
   } else {
-    // ---------------- epilogue: warps 2..5
+    // ---------------- epilogue: warps 2..9
     const int sub = warp & 3;  // TMEM lanes 32*sub .. 32*sub+31
+    const int half = (warp - 2) >> 2;  // column half of the tile
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x) {
@@ -246,7 +254,7 @@ __global__ void __launch_bounds__(192, 1)
       const int row = m0 + sub * 32 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); c++) {
         const int n = n0 + c * 32;
         if (n >= a.N) break;  // uniform across the warp
         uint32_t r[32];
@@ -339,7 +347,8 @@ static int set_attr_t() {
 
 template <int BN, int EPI>
 static int launch_t(const GemmPlan& p, cudaStream_t st) {
-  gemm_bf16_kernel<BN, EPI><<<p.grid, 192, GemmCfg<BN>::SMEM, st>>>(p.tmA, p.tmB, p.args);
+  gemm_bf16_kernel<BN, EPI><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, st>>>(p.tmA, p.tmB,
+                                                                             p.args);
   return check_launch("gemm_bf16");
 }
 

@@ -149,14 +149,13 @@ __global__ void __launch_bounds__(256) gelu_poly4_kernel(const void* __restrict_
     }
     uint16_t* dst = out + r * ld_out + c;
     if (VEC == 8) {
-      float y[8];
 #pragma unroll
-      for (int j = 0; j < 8; j++) y[j] = gelu_poly4<R>(x[j]);
+      for (int j = 0; j < 8; j += 2) gelu_poly4_x2<R>(x[j], x[j + 1]);
       uint4 o;
-      o.x = pack_bf16x2<R>(y[0], y[1]);
-      o.y = pack_bf16x2<R>(y[2], y[3]);
-      o.z = pack_bf16x2<R>(y[4], y[5]);
-      o.w = pack_bf16x2<R>(y[6], y[7]);
+      o.x = pack_bf16x2<R>(x[0], x[1]);
+      o.y = pack_bf16x2<R>(x[2], x[3]);
+      o.z = pack_bf16x2<R>(x[4], x[5]);
+      o.w = pack_bf16x2<R>(x[6], x[7]);
       *reinterpret_cast<uint4*>(dst) = o;
     } else {
       dst[0] = (uint16_t)bf16_bits<R>(gelu_poly4<R>(x[0]));
