@@ -333,6 +333,56 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
   return gemm_prepare(bn, epi);
 }
 
+// The same plan without the library's device error word, whose first use on
+// a device allocates it: the kernels' bounded waits then record nothing. Used
+// only by the allocation-free entry point (noalloc.cu).
+int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, const float* bias,
+                                 void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                 int64_t ldb, int64_t ldc, int epi) {
+  if (M <= 0 || N <= 0 || K <= 0) return fail(WX_ERR_INVALID, "gemm: M, N, K must be > 0");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(WX_ERR_UNSUPPORTED, "gemm: dimension exceeds 2^31");
+  if (!A || !B || !C) return fail(WX_ERR_INVALID, "gemm: NULL operand");
+  if (epi != WX_EPI_F32 && epi != WX_EPI_BF16 && epi != WX_EPI_BF16_GELU &&
+      epi != WX_EPI_BF16_GELU_ERF)
+    return fail(WX_ERR_INVALID, "gemm: epilogue %d", epi);
+  if (lda < K || ldb < K || ldc < N) return fail(WX_ERR_INVALID, "gemm: leading dimension too small");
+  if (lda % 8 || ldb % 8) return fail(WX_ERR_INVALID, "gemm: lda and ldb must be multiples of 8");
+  if (ldc % (epi == WX_EPI_F32 ? 4 : 8))
+    return fail(WX_ERR_INVALID, "gemm: ldc must keep rows 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(C) & 15) || (bias && (reinterpret_cast<uintptr_t>(bias) & 15)))
+    return fail(WX_ERR_INVALID, "gemm: C and bias must be 16-byte aligned");
+  const int nsm = sm_count();
+  const int64_t mb = (M + kGemmBM - 1) / kGemmBM;
+  const int bn = (mb * ((N + 255) / 256) >= nsm && N > 128) ? 256 : 128;  // as gemm_plan
+  WX_TRY(encode_tensor_map_2d(&p->tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
+                              (uint64_t)M, (uint64_t)lda * 2, kGemmBK, kGemmBM,
+                              CU_TENSOR_MAP_SWIZZLE_128B));
+  WX_TRY(encode_tensor_map_2d(&p->tmB, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
+                              (uint64_t)N, (uint64_t)ldb * 2, kGemmBK, (uint32_t)bn,
+                              CU_TENSOR_MAP_SWIZZLE_128B));
+  GemmArgs& g = p->args;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.num_n_blocks = (int)((N + bn - 1) / bn);
+  g.num_tiles = (int)(mb * g.num_n_blocks);
+  g.num_k_blocks = (int)((K + kGemmBK - 1) / kGemmBK);
+  g.C = C;
+  g.ldc = ldc;
+  g.bias = bias;
+  g.R = nullptr;
+  g.ldr = 0;
+  g.err = nullptr;
+  g.pos = nullptr;
+  g.ldp = 0;
+  g.pos_T = 1;
+  p->bn = bn;
+  p->epi = epi;
+  p->grid = g.num_tiles < nsm ? g.num_tiles : nsm;
+  return gemm_prepare(bn, epi);
+}
+
 template <int BN, int EPI>
 static int set_attr_t() {
   static bool done[64] = {false};

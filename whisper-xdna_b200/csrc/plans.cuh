@@ -37,6 +37,9 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
               void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
               int64_t ldr, int epi, int force_bn);
 int gemm_run(const GemmPlan& p, cudaStream_t st);
+int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, const float* bias,
+                                 void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                 int64_t ldb, int64_t ldc, int epi);
 // attach the positional embedding to a plan built with kEpiF32Gelu*Pos
 void gemm_set_pos(GemmPlan* p, const float* pos, int64_t ldp, int pos_T);
 

@@ -45,6 +45,7 @@ SIGNATURES = {
     "wx_gelu4_table": (_i, [_i, _p, _i64]),
     "wx_gemm_bf16": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p]),
     "wx_attention": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p]),
+    "wx_mlp_bf16_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),
     "wx_encoder_create": (_i, [_c.POINTER(_p), _i, _i, _i, _i, _i, _i, _i, _i]),
     "wx_encoder_destroy": (_i, [_p]),
     "wx_encoder_set_frontend": (_i, [_p, _p, _p, _p, _p, _p]),
