@@ -32,6 +32,10 @@ sys.path.insert(0, str(ROOT / "whisper-xdna_b200"))
 METRIC = "large-v3 encoder clips/s @ctx1500"
 UNIT = "clips/s"
 N_MELS, D, N_HEAD, N_LAYER, FFN, CTX = 128, 1280, 20, 32, 5120, 1500
+# DRAM bytes (read + write) of one attention launch per clip, measured by ncu
+# on a 4-clip launch (profiles/attention_ncu_b4.md: 46.14 MB read, 0.28 MB
+# written); Q, K and V are read once, O stays in L2 at that size.
+ATTN_DRAM_BYTES_PER_CLIP = (46.135e6 + 0.276e6) / 4
 FLOP_PER_CLIP = (N_LAYER * (8 * CTX * D * D + 4 * CTX * D * FFN + 4 * CTX * CTX * D)
                  + 2 * (2 * CTX) * (3 * N_MELS) * D + 2 * CTX * (3 * D) * D)
 
@@ -47,6 +51,18 @@ def parse():
     ap.add_argument("--cpu-layers", type=int, default=2,
                     help="layers in the bounded CPU sample")
     return ap.parse_args()
+
+
+def arm_config(batch, world):
+    """The workload both arms report (the reference arm times a bounded sample
+    of it)."""
+    return {"workload": f"large-v3 encoder forward, ctx 1500, {batch} clips per GPU per step "
+                        "(BASELINE batch-64 config, clip-sharded)",
+            "model": "whisper large-v3 encoder (32 layers, d 1280, 20x64 heads, ffn 5120)",
+            "global_batch": batch * world, "seq_len": CTX,
+            "parallelism": f"dp{world} (independent replicas, no collective)",
+            "gelu": "poly4 RNE (the reference's device GELU)",
+            "l2": "inputs larger than L2 (no flush)", "cuda_graph": True}
 
 
 # ------------------------------------------------------------------ CPU side
@@ -102,11 +118,10 @@ def run_reference(args, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "large-v3 encoder forward, ctx 1500, one clip per step "
-                               "(bounded sample)", "model": "large-v3 (random weights)",
-                   "global_batch": 1, "seq_len": CTX, "parallelism": "host cores"},
+        "config": arm_config(args.batch, args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
-                         "sample": desc},
+                         "sample": desc + "; the oracle port of the reference's numpy encoder, "
+                                          "all host threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
@@ -194,63 +209,25 @@ def make_weights_fast(seed):
 
 
 def kernel_rooflines(batch, peaks):
-    """Time the encoder's kernels one at a time with CUDA events on the
-    launching stream (inputs larger than L2), on this rank's shapes."""
-    import torch
-    from wxb200 import _lib as L
-    from wxb200 import ops
-    M = batch * CTX
-    dev = "cuda"
-    st = torch.cuda.current_stream()
-    g = torch.Generator(device=dev).manual_seed(7)
-    h = (torch.randn(M, D, device=dev, generator=g)).to(torch.bfloat16)
-    f = (torch.randn(M, FFN, device=dev, generator=g) * 0.5).to(torch.bfloat16)
-    qkv = torch.randn(M, 3 * D, device=dev, generator=g).to(torch.bfloat16)
-    x = torch.randn(M, D, device=dev, generator=g)
-    w1 = (torch.randn(FFN, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-    w2 = (torch.randn(D, FFN, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-    wqkv = (torch.randn(3 * D, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-    b1 = torch.zeros(FFN, device=dev)
-    b2 = torch.zeros(D, device=dev)
-    bq = torch.zeros(3 * D, device=dev)
-    o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
-    hb = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
-    ones = torch.ones(D, device=dev)
-    zeros = torch.zeros(D, device=dev)
-
-    def timed(fn, reps=10, warm=3):
-        for _ in range(warm):
-            fn()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record(st)
-        for _ in range(reps):
-            fn()
-        e1.record(st)
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / reps / 1e3
-
+    """Time the encoder's kernels one at a time (CUDA events on the launching
+    stream) at this rank's shapes, whose inputs are larger than L2, and the
+    standalone row ops at the BASELINE row-op sizes with L2 flushed between
+    launches (their inputs fit in L2)."""
+    from wxb200.kernel_bench import time_kernel
     res = {}
-    fl = 2.0 * M * D * FFN
-    t = timed(lambda: ops.gemm(h, w1, bias=b1, out=f, epilogue=L.WX_EPI_BF16_GELU))
-    res["gemm_fc1_gelu"] = {"s": t, "tflops": fl / t / 1e12}
-    t = timed(lambda: ops.gemm(f, w2, bias=b2, residual=x, out=x, epilogue=L.WX_EPI_F32_RESID))
-    res["gemm_fc2_resid"] = {"s": t, "tflops": fl / t / 1e12}
-    t = timed(lambda: ops.gemm(h, wqkv, bias=bq, out=qkv, epilogue=L.WX_EPI_BF16))
-    res["gemm_qkv"] = {"s": t, "tflops": 2.0 * M * D * 3 * D / t / 1e12}
-    af = 4.0 * batch * CTX * CTX * D
-    t = timed(lambda: ops.attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], batch, N_HEAD,
-                                    0.125, out=o), reps=5)
-    res["attention"] = {"s": t, "tflops": af / t / 1e12}
-    lb = M * D * (4 + 2) + 2 * D * 4
-    t = timed(lambda: ops.layer_norm_rows(x, ones, zeros, out=hb, mode=L.WX_LN_FP32))
-    res["layernorm_f32_bf16"] = {"s": t, "gbs": lb / t / 1e9}
-    for k, v in res.items():
-        if "tflops" in v:
-            v["frac_of_measured_bf16"] = v["tflops"] * 1e12 / (peaks["bf16_tflops"] * 1e12)
+    for k in ("attention", "fc1", "fc2", "qkv", "outproj", "layernorm"):
+        r = time_kernel(k, batch=batch, iters=5 if k == "attention" else 10)
+        if r["flop"]:
+            r["frac_of_measured_bf16"] = r["tflops"] / peaks["bf16_tflops"]
         else:
-            v["frac_of_measured_hbm"] = v["gbs"] / peaks["hbm_gbs"]
-    return res
+            r["frac_of_measured_hbm"] = r["gbs"] / peaks["hbm_gbs"]
+        res[k] = r
+    rows = {}
+    for k in ("gelu", "gelu_f32", "softmax", "layernorm_gb"):
+        r = time_kernel(k, iters=20, flush=True)
+        r["frac_of_measured_hbm"] = r["gbs"] / peaks["hbm_gbs"]
+        rows[k] = r
+    return res, rows
 
 
 def load_peaks():
@@ -283,16 +260,9 @@ def run_b200(args, rank, world, local_rank):
     out = torch.empty(B, CTX, D, device="cuda")
     st = torch.cuda.current_stream()
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    from wxb200 import dist as wdist
+    barrier = wdist.barrier
+    max_over_ranks = wdist.max_over_ranks
 
     # ---- device-resident timing
     for _ in range(args.warmup):
@@ -332,15 +302,18 @@ def run_b200(args, rank, world, local_rank):
     e2e = total_clips / t_e2e
     peaks = load_peaks()
     roof, cpu = None, None
-    kernels = {}
+    kernels, row_ops = {}, {}
     if rank == 0:
-        kernels = kernel_rooflines(B, peaks)
-        k = kernels["gemm_fc1_gelu"]
-        fl = 2.0 * B * CTX * D * FFN
-        roof = {"bound": "tensor", "kernel": "gemm_bf16_kernel<256, BF16_GELU> (fc1 + GELU)",
+        kernels, row_ops = kernel_rooflines(B, peaks)
+        # the dominant kernel of the launch list (profiles/launches_encoder_b64.md)
+        k = kernels["attention"]
+        roof = {"bound": "tensor", "kernel": "attention_kernel (fused QK^T-softmax-PV, 20 heads)",
                 "achieved": k["tflops"], "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": k["tflops"] / peaks["bf16_tflops"], "peak_source": peaks["src"],
-                "flop_per_launch": fl, "traffic": None,
+                "flop_per_launch": 4.0 * B * CTX * CTX * D,
+                "traffic": ATTN_DRAM_BYTES_PER_CLIP * B,
+                "traffic_note": "dram read+write per launch, from the ncu capture in "
+                                "profiles/attention_ncu_b4.md scaled by clips (4 -> B)",
                 "whole_step": {"achieved": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12,
                                "frac": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12
                                / peaks["bf16_tflops"]}}
@@ -357,19 +330,12 @@ def run_b200(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (random N(0,0.02) large-v3 weights, "
                                      "U[-0.8,1.2] log-mel per clip)",
-            "config": {"workload": f"large-v3 encoder forward, ctx 1500, {B} clips per GPU "
-                                   "per step (BASELINE batch-64 config, clip-sharded)",
-                       "model": "whisper large-v3 encoder (32 layers, d 1280, 20x64 heads, "
-                                "ffn 5120)",
-                       "global_batch": B * world, "seq_len": CTX,
-                       "parallelism": f"dp{world} (independent replicas, no collective)",
-                       "gelu": "poly4 RNE (the reference's device GELU)",
-                       "l2": "inputs larger than L2 (no flush)", "cuda_graph": True},
+            "config": arm_config(B, world),
             "e2e": {"value": e2e, "unit": UNIT,
                     "h2d_bytes_per_step": int(mel_host.numel() * 4),
                     "d2h_bytes_per_step": int(out_host.numel() * 4)},
             "gpu_launches": (2 + 2 + 7 * N_LAYER + 1) * args.steps,
-            "roofline": roof, "kernels": kernels, "clocks": clk,
+            "roofline": roof, "kernels": kernels, "row_ops": row_ops, "clocks": clk,
             "cpu_baseline": cpu, "output_finite": finite,
             "flop_per_clip": FLOP_PER_CLIP,
         }

@@ -1,0 +1,128 @@
+"""Time one kernel of the hot path at the encoder's shapes, through the C ABI.
+
+    PYTHONPATH=whisper-xdna_b200 python -m wxb200.kernel_bench --kernel attention --batch 4
+
+Kernels: attention, fc1 (GEMM + GELU), fc2 (GEMM + residual), qkv, outproj,
+layernorm (fp32 -> bf16, the encoder's), and the standalone row ops at the
+BASELINE row-op sizes: gelu (g4r 1500x5120), gelu_f32 (g4f 1500x5120), softmax
+(s4r 20x1500x1500, scale 1/8), layernorm_gb (1500x1280 with gamma/beta).
+Each launch is timed with CUDA events on the launching stream after warm-up;
+with --flush the L2 (126 MB) is overwritten between launches, which the row
+ops need since their inputs fit in L2. Prints one JSON line.
+"""
+import argparse
+import json
+
+import torch
+
+from . import _lib as L
+from . import ops
+
+D, H, FFN, T = 1280, 20, 5120, 1500
+
+
+def setup(kernel, batch, dev="cuda"):
+    """Return (fn, flop_per_launch, bytes_per_launch) for one kernel."""
+    g = torch.Generator(device=dev).manual_seed(0)
+    M = batch * T
+    rn = lambda *s, sc=1.0: (torch.randn(*s, device=dev, generator=g) * sc)
+    if kernel == "attention":
+        qkv = rn(M, 3 * D).to(torch.bfloat16)
+        o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+        fn = lambda: ops.attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], batch, H, 0.125,
+                                   out=o)
+        return fn, 4.0 * batch * T * T * D, 4.0 * M * D * 2
+    if kernel in ("fc1", "fc2", "qkv", "outproj"):
+        K, N = {"fc1": (D, FFN), "fc2": (FFN, D), "qkv": (D, 3 * D), "outproj": (D, D)}[kernel]
+        A = rn(M, K).to(torch.bfloat16)
+        W = rn(N, K, sc=0.02).to(torch.bfloat16)
+        b = torch.zeros(N, device=dev)
+        if kernel in ("fc2", "outproj"):
+            x = rn(M, N)
+            fn = lambda: ops.gemm(A, W, bias=b, residual=x, out=x, epilogue=L.WX_EPI_F32_RESID)
+            byt = M * K * 2 + N * K * 2 + 2 * M * N * 4
+        else:
+            C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            epi = L.WX_EPI_BF16_GELU if kernel == "fc1" else L.WX_EPI_BF16
+            fn = lambda: ops.gemm(A, W, bias=b, out=C, epilogue=epi)
+            byt = M * K * 2 + N * K * 2 + M * N * 2
+        return fn, 2.0 * M * N * K, byt
+    if kernel == "layernorm":
+        x = rn(M, D)
+        h = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+        gm, bt = torch.ones(D, device=dev), torch.zeros(D, device=dev)
+        fn = lambda: ops.layer_norm_rows(x, gm, bt, out=h, mode=L.WX_LN_FP32)
+        return fn, 0.0, M * D * (4 + 2) + 2 * D * 4
+    # standalone row ops, BASELINE sizes (batch ignored)
+    if kernel == "gelu":
+        x = (rn(1500, 5120) * 3).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        return (lambda: ops.gelu_poly4(x, out=y, rounding=L.WX_ROUND_RNE)), 0.0, x.numel() * 4
+    if kernel == "gelu_f32":
+        x = rn(1500, 5120) * 3
+        y = torch.empty(1500, 5120, device=dev, dtype=torch.bfloat16)
+        return (lambda: ops.gelu_poly4(x, out=y, rounding=L.WX_ROUND_RNE)), 0.0, x.numel() * 6
+    if kernel == "softmax":
+        x = (rn(20 * 1500, 1500) * 3).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        fn = lambda: ops.softmax_rows(x, out=y, scale=0.125, variant=4, rounding=L.WX_ROUND_RNE)
+        return fn, 0.0, x.numel() * 4
+    if kernel == "layernorm_gb":
+        x = (rn(1500, 1280) * 3).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        gm, bt = rn(1280, sc=0.1) + 1, rn(1280, sc=0.1)
+        fn = lambda: ops.layer_norm_rows(x, gm, bt, out=y, mode=L.WX_LN_AIE,
+                                         rounding=L.WX_ROUND_RNE)
+        return fn, 0.0, x.numel() * 4 + 2 * 1280 * 4
+    raise ValueError(f"unknown kernel {kernel!r}")
+
+
+def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False):
+    fn, flop, byt = setup(kernel, batch)
+    junk = torch.empty(256 * 1024 * 1024 // 4, device="cuda") if flush else None
+    st = torch.cuda.current_stream()
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    if flush:
+        for _ in range(iters):
+            junk.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1) / 1e3
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(iters):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        total = e0.elapsed_time(e1) / 1e3
+    t = total / iters
+    res = {"kernel": kernel, "batch": batch, "s": t, "flop": flop, "bytes": byt,
+           "flush_l2": bool(flush)}
+    if flop:
+        res["tflops"] = flop / t / 1e12
+    res["gbs"] = byt / t / 1e9
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default="attention")
+    ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--flush", action="store_true")
+    a = ap.parse_args()
+    res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush)
+    res["device_error"] = L.device_error()
+    print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()
