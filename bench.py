@@ -105,6 +105,13 @@ def cpu_cores():
 def run_reference(args, rank):
     if rank != 0:
         return
+    # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
     for _ in range(args.warmup):
         cpu_sample(1)
     vals, spent, desc = [], 0.0, ""

@@ -3,7 +3,7 @@
 // QK -> softmax -> AV chain of the reference in one kernel, with the scores
 // never leaving the SM.
 //
-// One CTA per (pair of 128-query tiles A and B, head, clip); 10 warps:
+// One CTA per (pair of 128-query tiles A and B, head, clip); 18 warps:
 //   warp 0     TMA: the two Q tiles once, then K and V tiles (128 keys x 64)
 //              into two-slot rings with separate K and V barriers
 //   warp 1     allocates tensor memory and issues, per key block j,
@@ -11,11 +11,16 @@
 //              (M=128; S: N=128, K=64; PV: N=64, K=128 with V read MN-major
 //              straight from its row-major tile), O accumulating in tensor
 //              memory across blocks
-//   warps 2-5  softmax of tile A, warps 6-9 of tile B, one query row per
-//              thread: the S row is loaded from tensor memory once and the
-//              buffer released at once, so the next QK^T overlaps this block's
-//              exponentials; P = exp2(s*c - m) goes to shared memory as bf16 in
-//              the 128-byte-swizzled K-major layout the PV MMA reads.
+//   warps 2-9  softmax of tile A, warps 10-17 of tile B. A query row is split
+//              over two warps of one tensor-memory sub-partition (keys 0-63
+//              and 64-127 of each block; O columns 0-31 and 32-63), which puts
+//              four softmax warps on every SM sub-partition; the two halves
+//              exchange their partial row maxima through shared memory at a
+//              64-thread named barrier once per block and their row sums once
+//              at the end. Each S half-row is loaded from tensor memory once
+//              and the buffer released at once, so the next QK^T overlaps this
+//              block's exponentials; P = exp2(s*c - m) goes to shared memory as
+//              bf16 in the 128-byte-swizzled K-major layout the PV MMA reads.
 // The two tiles' softmax warpgroups alternate with each other's MMAs.
 //
 // Online softmax with lazy rescaling: the running max m only moves when a
@@ -28,6 +33,8 @@
 // c = exp(m - m'), l' = c l + rowsum exp(S - m'), O' = c O + exp(S - m') V.
 // Keys past T are masked exactly (p = 0); the reference's zero-padded keys
 // took probability mass (src/rawxrt.py:618-623), which is not reproduced.
+#include <type_traits>
+
 #include "common.cuh"
 #include "plans.cuh"
 
@@ -36,11 +43,12 @@ namespace wx {
 constexpr int kAttBQ = 128;                       // rows per Q tile (2 tiles per CTA)
 constexpr int kAttBK = 128;                       // keys per block
 constexpr int kAttHD = 64;
-constexpr int kAttThreads = 320;
+constexpr int kAttThreads = 576;   // 2 control warps + 16 softmax warps
 constexpr int kTileBytes = 128 * kAttHD * 2;      // 16 KB: Q, K or V tile
 constexpr int kPBytes = kAttBQ * kAttBK * 2;      // 32 KB: P tile
-// Q_A, Q_B, K x2, V x2, P_A, P_B
-constexpr int kAttSmem = 1024 + kTileBytes * 6 + kPBytes * 2 + 512;
+// Q_A, Q_B, K x2, V x2, P_A, P_B, barriers, the row-max exchange (2 tiles x 2
+// parities x 2 halves x 128 rows of fp32)
+constexpr int kAttSmem = 1024 + kTileBytes * 6 + kPBytes * 2 + 256 + 2 * 2 * 2 * 128 * 4;
 constexpr int kAttTmemCols = 512;
 constexpr int kSCol = 0;      // S_A at 0, S_B at 128
 constexpr int kOCol = 256;    // O_A at 256, O_B at 320
@@ -63,7 +71,7 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// 10 warps: three share a sub-partition's 16K registers, so at most 168 each.
+// 18 warps: five share a sub-partition's 16K registers, so at most 96 each.
 __global__ void __launch_bounds__(kAttThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmK,
@@ -103,8 +111,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&s_empty[i], 256);
+      mbar_init(&p_full[i], 256);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(done, 1);
@@ -155,7 +163,10 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---------------- MMA issuer
+      // ---------------- MMA issuer. Order per block j: S_A(j+1), PV_A(j),
+      // S_B(j+1), PV_B(j). The waits are blocking mbarrier try-waits, which
+      // suspend the warp instead of taking issue slots from the softmax warps
+      // that share its sub-partition (a polling scheduler measured slower).
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kAttBQ, kAttBK, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(kAttBQ, kAttHD, 0, 1);
       bool ok = mbar_wait(q_full, 0, a.err);
@@ -206,33 +217,38 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       mbar_wait_for(done, 0, kWaitTimeoutNs);
     }
   } else {
-    // ---------------- softmax: warps 2-5 tile A, 6-9 tile B; thread <-> row
-    const int t = (warp - 2) >> 2;
+    // ---------------- softmax: warps 2-9 tile A, 10-17 tile B. Each query row
+    // is split over two warps of the same TMEM sub-partition: half 0 takes keys
+    // 0-63 of every block and O columns 0-31, half 1 keys 64-127 and O 32-63.
+    const int t = (warp - 2) >> 3;
+    const int half = ((warp - 2) & 7) >> 2;
     const int sub = warp & 3;
     const int r = sub * 32 + lane;  // row within the tile
     const uint32_t t_lane = tmem + ((uint32_t)(sub * 32) << 16);
-    const uint32_t t_s = t_lane + kSCol + t * kAttBK;
-    const uint32_t t_o = t_lane + kOCol + t * kAttHD;
-    uint8_t* prow = sP + t * kPBytes + r * 128;
+    const uint32_t t_s = t_lane + kSCol + t * kAttBK + half * 64;
+    const uint32_t t_o = t_lane + kOCol + t * kAttHD + half * 32;
+    uint8_t* prow = sP + t * kPBytes + half * (kPBytes / 2) + r * 128;
+    // partial row maxima of the two halves, double-buffered by block parity
+    float* xchg = reinterpret_cast<float*>(bars + 20) + t * 2 * 2 * 128;  // [parity][half][row]
+    const int bar_id = 1 + t * 4 + sub;  // named barrier of the warp pair
     const float c = a.scale_log2;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv; j++) {
-      const int kvalid = min(kAttBK, T - j * kAttBK);
-      if (!mbar_wait(&s_full[t], j & 1, a.err)) { ok = false; break; }
+      const int kvalid = min(kAttBK, T - j * kAttBK) - half * 64;  // valid keys of this half
+      // A failed wait never leaves the loop: the two halves of a row meet at
+      // named barriers (which have no time limit) once per block, so both run
+      // every iteration; once the error word is set the remaining waits return
+      // at once.
+      if (!mbar_wait(&s_full[t], j & 1, a.err)) ok = false;
       tc_fence_after();
-      // the S row as four 32-column register arrays (separate arrays keep
-      // them in registers)
-      uint32_t s0[32], s1[32], s2[32], s3[32];
+      uint32_t s0[32], s1[32];
       tmem_ld32(t_s + 0, s0);
       tmem_ld32(t_s + 32, s1);
-      tmem_ld32(t_s + 64, s2);
-      tmem_ld32(t_s + 96, s3);
       tmem_wait_ld();
       // S is in registers: the next QK^T may overwrite the buffer
       tc_fence_before();
       mbar_arrive(&s_empty[t]);
-      // row max over the valid keys as a tree (short dependency chains)
       auto chunk_max = [&](const uint32_t (&v)[32], int base) -> float {
         float mm[8];
         if (kvalid >= base + 32) {
@@ -252,55 +268,61 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         return fmaxf(fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3])),
                      fmaxf(fmaxf(mm[4], mm[5]), fmaxf(mm[6], mm[7])));
       };
-      float mx = fmaxf(fmaxf(chunk_max(s0, 0), chunk_max(s1, 32)),
-                       fmaxf(chunk_max(s2, 64), chunk_max(s3, 96)));
-      mx *= c;
+      float mx = fmaxf(chunk_max(s0, 0), chunk_max(s1, 32));
+      // combine with the other half of the row
+      float* slot = xchg + (j & 1) * 256;
+      slot[half * 128 + r] = mx;
+      asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(64) : "memory");
+      mx = fmaxf(mx, slot[(half ^ 1) * 128 + r]) * c;
       const bool grow = mx > m + kRescaleThreshold;  // includes the first block
       const float m_use = grow ? mx : m;
       const float corr = fast_exp2(m - m_use);        // 1 when m stays, 0 on block 0
       // P_t(j-1) V must have been consumed before P is rewritten (and before
       // O is rescaled)
-      if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, a.err)) { ok = false; break; }
+      if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, a.err)) ok = false;
       m = m_use;
       float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent accumulators
       const float negm = -m;
-      // 32 keys = 4 chunks of 8 keys (16 bytes each) of the swizzled P row
-      auto chunk_p = [&](const uint32_t (&v)[32], int base) {
+      // 32 keys = 4 chunks of 8 keys (16 bytes each) of the swizzled P row;
+      // MASKED only for the last, partial key block
+      auto chunk_p = [&](const uint32_t (&v)[32], int base, auto masked) {
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; e++) {
             const int i = q * 8 + 2 * e;
-            const float p0 =
-                (base + i < kvalid) ? fast_exp2(fmaf(__uint_as_float(v[i]), c, negm)) : 0.0f;
-            const float p1 =
-                (base + i + 1 < kvalid) ? fast_exp2(fmaf(__uint_as_float(v[i + 1]), c, negm)) : 0.0f;
+            float p0 = fast_exp2(fmaf(__uint_as_float(v[i]), c, negm));
+            float p1 = fast_exp2(fmaf(__uint_as_float(v[i + 1]), c, negm));
+            if (decltype(masked)::value) {
+              p0 = (base + i < kvalid) ? p0 : 0.0f;
+              p1 = (base + i + 1 < kvalid) ? p1 : 0.0f;
+            }
             w[e] = pack_bf16x2_rne(p0, p1);
             sums[e] += p0 + p1;
           }
-          const int chunk = base / 8 + q;  // 16-byte chunk index along the row (0..15)
-          uint8_t* dst = prow + (chunk >> 3) * (kPBytes / 2) + (((chunk & 7) ^ (r & 7)) << 4);
+          const int chunk = base / 8 + q;  // 16-byte chunk within this half's 128-byte row
+          uint8_t* dst = prow + ((chunk ^ (r & 7)) << 4);
           *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       };
-      chunk_p(s0, 0);
-      chunk_p(s1, 32);
-      chunk_p(s2, 64);
-      chunk_p(s3, 96);
+      if (kvalid >= 64) {
+        chunk_p(s0, 0, std::false_type());
+        chunk_p(s1, 32, std::false_type());
+      } else {
+        chunk_p(s0, 0, std::true_type());
+        chunk_p(s1, 32, std::true_type());
+      }
       // O rescale after P is written, so the S registers are free; PV(j) reads
       // O only after p_full below
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         tc_fence_after();
         uint32_t ov[32];
+        tmem_ld32(t_o, ov);
+        tmem_wait_ld();
 #pragma unroll
-        for (int half = 0; half < 2; half++) {
-          tmem_ld32(t_o + half * 32, ov);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; i++) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
-          tmem_st32(t_o + half * 32, ov);
-        }
+        for (int i = 0; i < 32; i++) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
+        tmem_st32(t_o, ov);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -309,30 +331,29 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       l = l * corr + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
     }
     if (ok) ok = mbar_wait(&o_done[t], (nkv - 1) & 1, a.err);
+    // the row sum is the sum of the two halves' sums
+    float* lslot = xchg + (nkv & 1) * 256;
+    lslot[half * 128 + r] = l;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(64) : "memory");
+    l += lslot[(half ^ 1) * 128 + r];
     if (ok) {
       tc_fence_after();
-      uint32_t o0[32], o1[32];
+      uint32_t o0[32];
       tmem_ld32(t_o, o0);
-      tmem_ld32(t_o + 32, o1);
       tmem_wait_ld();
       const int qrow = q0 + t * kAttBQ + r;
       if (qrow < T) {
         const float inv = 1.0f / l;
         uint16_t* dst = reinterpret_cast<uint16_t*>(a.O) + (int64_t)(row0 + qrow) * a.ldo +
-                        h * kAttHD;
+                        h * kAttHD + half * 32;
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
-          uint4 w0, w1;
+          uint4 w0;
           w0.x = pack_bf16x2_rne(__uint_as_float(o0[i]) * inv, __uint_as_float(o0[i + 1]) * inv);
           w0.y = pack_bf16x2_rne(__uint_as_float(o0[i + 2]) * inv, __uint_as_float(o0[i + 3]) * inv);
           w0.z = pack_bf16x2_rne(__uint_as_float(o0[i + 4]) * inv, __uint_as_float(o0[i + 5]) * inv);
           w0.w = pack_bf16x2_rne(__uint_as_float(o0[i + 6]) * inv, __uint_as_float(o0[i + 7]) * inv);
-          w1.x = pack_bf16x2_rne(__uint_as_float(o1[i]) * inv, __uint_as_float(o1[i + 1]) * inv);
-          w1.y = pack_bf16x2_rne(__uint_as_float(o1[i + 2]) * inv, __uint_as_float(o1[i + 3]) * inv);
-          w1.z = pack_bf16x2_rne(__uint_as_float(o1[i + 4]) * inv, __uint_as_float(o1[i + 5]) * inv);
-          w1.w = pack_bf16x2_rne(__uint_as_float(o1[i + 6]) * inv, __uint_as_float(o1[i + 7]) * inv);
           *reinterpret_cast<uint4*>(dst + i) = w0;
-          *reinterpret_cast<uint4*>(dst + 32 + i) = w1;
         }
       }
     }

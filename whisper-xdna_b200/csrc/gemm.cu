@@ -251,6 +251,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m0 = (tile / nnb) * kGemmBM, n0 = (tile % nnb) * BN;
       if (!mbar_wait(&tfull[acc], acc_phase, a.err)) break;
       tc_fence_after();
+      if (EPI == WX_EPI_F32_RESID) {
+        // the residual rows of this warp's next tile, into L2 while this tile drains
+        const int nt = tile + gridDim.x;
+        if (nt < a.num_tiles) {
+          const int prow = (nt / nnb) * kGemmBM + sub * 32 + lane;
+          const int pn = (nt % nnb) * BN + half * (BN / 2);
+          if (prow < a.M) {
+            const float* base = a.R + (int64_t)prow * a.ldr + pn;
+#pragma unroll
+            for (int q = 0; q < BN / 64; q++)
+              if (pn + q * 32 < a.N) prefetch_l2(base + q * 32);
+          }
+        }
+      }
       const int row = m0 + sub * 32 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
