@@ -77,32 +77,38 @@ __device__ __forceinline__ void rbf2(float& a, float& b) {
 }
 
 // GELU-poly4 of two bf16 values (kernels/gelu_poly4_eval.inc:27-65). The
-// piece is selected, not branched on: every element runs one Horner chain
-// with the coefficients of its piece, and elements past the last break keep
-// q = 0 whatever that chain computed, so the compiler can interleave the
-// chains of many elements.
+// piece is selected, not branched on, so the compiler can interleave the
+// chains of many elements: with pa = [s < 1] and pb = [1 <= s < 2] as 0/1
+// floats, every coefficient is C2 + pa*(C0 - C2) + pb*(C1 - C2) by two FMAs
+// (the differences of bf16 coefficients are exact in fp32, so the selection is
+// exact), the shift 3 - 2.5*pa - 1.5*pb likewise, and the scale 1 + pa + pb is
+// 1 or 2, so u = R(s - shift) * scale needs no second rounding. This keeps the
+// selection on the FMA pipe (the ALU pipe carries the bf16 roundings); it was
+// checked on every bf16 input against the reference's evaluation order.
+// Elements past the last break keep q = 0 whatever their chain computed.
 template <int R>
 __device__ __forceinline__ void gelu_poly4_x2(float& x0, float& x1) {
   constexpr float kC[3][5] = WX_GELU4_COEF;
   const float s0 = fabsf(x0), s1 = fabsf(x1);    // s = max(x, 0 - x)
-  const bool a0 = s0 < 1.0f, b0 = s0 < 2.0f, in0 = s0 < 4.0f;
-  const bool a1 = s1 < 1.0f, b1 = s1 < 2.0f, in1 = s1 < 4.0f;
-  float t0 = s0 - (a0 ? 0.5f : (b0 ? 1.5f : 3.0f));
-  float t1 = s1 - (a1 ? 0.5f : (b1 ? 1.5f : 3.0f));
+  const float pa0 = s0 < 1.0f ? 1.0f : 0.0f, pa1 = s1 < 1.0f ? 1.0f : 0.0f;
+  const float pb0 = (s0 < 2.0f ? 1.0f : 0.0f) - pa0, pb1 = (s1 < 2.0f ? 1.0f : 0.0f) - pa1;
+  float t0 = s0 - fmaf(pa0, -2.5f, fmaf(pb0, -1.5f, 3.0f));
+  float t1 = s1 - fmaf(pa1, -2.5f, fmaf(pb1, -1.5f, 3.0f));
   rbf2<R>(t0, t1);                                // bf16 sub
-  float u0 = t0 * (b0 ? 2.0f : 1.0f), u1 = t1 * (b1 ? 2.0f : 1.0f);
-  rbf2<R>(u0, u1);                                // bf16 mul
-  float acc0 = a0 ? kC[0][0] : (b0 ? kC[1][0] : kC[2][0]);
-  float acc1 = a1 ? kC[0][0] : (b1 ? kC[1][0] : kC[2][0]);
+  const float u0 = t0 * (1.0f + pa0 + pb0), u1 = t1 * (1.0f + pa1 + pb1);  // exact
+  auto coef = [&](int k, float pa, float pb) {
+    return fmaf(pa, kC[0][k] - kC[2][k], fmaf(pb, kC[1][k] - kC[2][k], kC[2][k]));
+  };
+  float acc0 = coef(0, pa0, pb0), acc1 = coef(0, pa1, pb1);
 #pragma unroll
   for (int k = 1; k < 5; k++) {                   // Horner, fp32 MAC, bf16 state
     rbf2<R>(acc0, acc1);
-    acc0 = fmaf(acc0, u0, a0 ? kC[0][k] : (b0 ? kC[1][k] : kC[2][k]));
-    acc1 = fmaf(acc1, u1, a1 ? kC[0][k] : (b1 ? kC[1][k] : kC[2][k]));
+    acc0 = fmaf(acc0, u0, coef(k, pa0, pb0));
+    acc1 = fmaf(acc1, u1, coef(k, pa1, pb1));
   }
   rbf2<R>(acc0, acc1);
-  float r0 = ((x0 >= 0.0f) ? x0 : 0.0f) + (in0 ? acc0 : 0.0f);   // relu(x) + q
-  float r1 = ((x1 >= 0.0f) ? x1 : 0.0f) + (in1 ? acc1 : 0.0f);
+  float r0 = ((x0 >= 0.0f) ? x0 : 0.0f) + (s0 < 4.0f ? acc0 : 0.0f);   // relu(x) + q
+  float r1 = ((x1 >= 0.0f) ? x1 : 0.0f) + (s1 < 4.0f ? acc1 : 0.0f);
   rbf2<R>(r0, r1);
   x0 = r0;
   x1 = r1;

@@ -246,6 +246,31 @@ __device__ __forceinline__ float exp_lookup(float x, float m, const uint16_t* t1
 }
 
 // ---------------------------------------------------------------- softmax
+// e = R(exp(R(x - max))) as the table holds it (the correctly rounded fp32
+// exponential, then bf16 in mode R), computed on the SFU: exp2(d * log2 e)
+// carries a relative error below 2^-17 (argument rounding 2^-18 for |d| <= 87,
+// the log2 e constant 2^-18, ex2.approx 2^-22), i.e. under 64 fp32 ulps, so
+// wherever the approximate value lies more than 1024 ulps from a bf16
+// rounding boundary it rounds to the same bf16 as the exact one. Near a
+// boundary, below -87 (subnormal results) or at d = 0 the table decides.
+template <int R>
+__device__ __forceinline__ uint32_t exp_bits_checked(float x, float m, const uint16_t* t16) {
+  constexpr uint32_t kMargin = 1024;
+  const float d = rbf<R>(__fsub_rn(x, m));
+  const uint32_t b = __float_as_uint(d) >> 16;
+  if (d > -87.0f && b != 0u && b != 0x8000u) {
+    const float e = fast_exp2(__fmul_rn(d, 1.44269504f));
+    const uint32_t lo = __float_as_uint(e) & 0xFFFFu;
+    const bool near = (R == RND_RNE) ? (lo + kMargin - 0x8000u <= 2 * kMargin)
+                                     : (lo <= kMargin || lo >= 0x10000u - kMargin);
+    if (!near) return bf16_bits<R>(e);
+  }
+  if (b == 0u || b == 0x8000u) return 0x3F80u;  // exp(0) = 1
+  if (b >= (uint32_t)kExpTabBase && b < (uint32_t)(kExpTabBase + kExpTabN))
+    return t16[b - kExpTabBase];
+  return 0u;
+}
+
 template <int R, int VAR>
 __global__ void __launch_bounds__(256) softmax_rows_kernel(
     const uint16_t* __restrict__ in, uint16_t* __restrict__ out, int64_t rows, int w,
@@ -269,12 +294,33 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(
     // pass 1: stage the window, row max seeded with (bfloat16)-30000 (body.inc:22-28)
     const float m = stage_row<R>(in + row * ld_in, buf, w, vec_in, do_scale, scale, -29952.0f, true);
     __syncwarp();
+    if (VAR != 3) {
+      // the exponentials, once, in place of the staged inputs (all 32 lanes)
+      const int nv = (w % 8 == 0) ? w / 8 : 0;
+      for (int v = lane; v < nv; v += 32) {
+        uint4 q = reinterpret_cast<const uint4*>(buf)[v];
+        uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          wd[j] = exp_bits_checked<R>(__uint_as_float(wd[j] << 16), m, t16) |
+                  (exp_bits_checked<R>(__uint_as_float(wd[j] & 0xFFFF0000u), m, t16) << 16);
+        reinterpret_cast<uint4*>(buf)[v] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      }
+      for (int c = nv * 8 + lane; c < w; c += 32)
+        buf[c] = (uint16_t)exp_bits_checked<R>(bits_f32(buf[c]), m, t16);
+      __syncwarp();
+    }
     // pass 2: 16 fp32 lanes, lane l summing e over columns l, l+16, ... (body.inc:31-40)
     float acc = 0.0f;
     if (lane < 16) {
       for (int c = lane; c < w; c += 16) {
-        float ea;
-        const float e = exp_lookup<R, false>(bits_f32(buf[c]), m, t16, t32, &ea);
+        float e;
+        if (VAR != 3) {
+          e = bits_f32(buf[c]);
+        } else {
+          float ea;
+          e = exp_lookup<R, false>(bits_f32(buf[c]), m, t16, t32, &ea);
+        }
         acc = __fadd_rn(acc, e);
       }
     }
@@ -284,8 +330,9 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(
     const float ilo = rbf<R>(__fsub_rn(inv, ihi));
     // pass 3: p = R(e*hi + e*lo) (body.inc:51-60), or the v1 / v3 forms
     auto prob = [&](float x) -> float {
-      float ea;
-      const float e = exp_lookup<R, N32>(x, m, t16, t32, &ea);
+      float ea = 0.0f, e;
+      if (VAR != 3) e = x;  // buf already holds e
+      else e = exp_lookup<R, N32>(x, m, t16, t32, &ea);
       if (VAR == 1) return rbf<R>(__fmul_rn(e, ihi));       // softmax_row.cc:50-57
       if (VAR == 3) {                                       // softmax_row3.cc:76-84
         const float ehi = rbf<R>(ea);
@@ -388,14 +435,14 @@ __global__ void __launch_bounds__(256) layernorm_aie_kernel(
   }
 }
 
-// fp32 two-pass LayerNorm, one warp per row; the row is kept in registers for
-// widths up to 2048 (NV = 16 float4 per lane), re-read from L2 beyond that.
-template <bool IN_BF16, bool OUT_BF16>
+// fp32 two-pass LayerNorm, one warp per row; the row is kept in registers as
+// NV float4 per lane (NV * 128 >= width; NV = 0: any width, re-read from L2).
+template <bool IN_BF16, bool OUT_BF16, int NV>
 __global__ void __launch_bounds__(256) layernorm_fp32_kernel(
     const void* __restrict__ in, const float* __restrict__ gamma,
     const float* __restrict__ beta, void* __restrict__ out, int64_t rows, int w, int64_t ld_in,
     int64_t ld_out, float eps) {
-  constexpr int NV = 16;
+  constexpr int NR = NV > 0 ? NV : 1;
   const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
   auto load4 = [&](int64_t row, int c) -> float4 {
     if (IN_BF16) {
@@ -409,29 +456,27 @@ __global__ void __launch_bounds__(256) layernorm_fp32_kernel(
   };
   for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
        row += (int64_t)gridDim.x * warps) {
-    float4 v[NV];
+    float4 v[NR];
     float s = 0.0f;
-    const bool fits = w <= NV * 128;
+    if (NV > 0) {
 #pragma unroll
-    for (int i = 0; i < NV; i++) {
-      const int c = (i * 32 + lane) * 4;
-      if (fits && c < w) {
-        v[i] = load4(row, c);
-        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-      } else {
-        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < NR; i++) {
+        const int c = (i * 32 + lane) * 4;
+        v[i] = c < w ? load4(row, c) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    }
-    if (!fits)
+#pragma unroll
+      for (int i = 0; i < NR; i++) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    } else {
       for (int c = lane * 4; c < w; c += 128) {
         const float4 t = load4(row, c);
         s += (t.x + t.y) + (t.z + t.w);
       }
+    }
     const float mean = warp_sum(s) / (float)w;
     float q = 0.0f;
-    if (fits) {
+    if (NV > 0) {
 #pragma unroll
-      for (int i = 0; i < NV; i++) {
+      for (int i = 0; i < NR; i++) {
         const int c = (i * 32 + lane) * 4;
         if (c < w) {
           const float a = v[i].x - mean, b = v[i].y - mean, d = v[i].z - mean, e = v[i].w - mean;
@@ -463,9 +508,9 @@ __global__ void __launch_bounds__(256) layernorm_fp32_kernel(
             make_float4(y0, y1, y2, y3);
       }
     };
-    if (fits) {
+    if (NV > 0) {
 #pragma unroll
-      for (int i = 0; i < NV; i++) {
+      for (int i = 0; i < NR; i++) {
         const int c = (i * 32 + lane) * 4;
         if (c < w) emit(c, v[i]);
       }
@@ -473,6 +518,23 @@ __global__ void __launch_bounds__(256) layernorm_fp32_kernel(
       for (int c = lane * 4; c < w; c += 128) emit(c, load4(row, c));
     }
   }
+}
+
+template <bool IB, bool OB>
+static void launch_ln_fp32(int grid, cudaStream_t st, const void* in, const float* gamma,
+                           const float* beta, void* out, int64_t rows, int w, int64_t ld_in,
+                           int64_t ld_out, float eps) {
+  const int nv = (w + 127) / 128;
+#define WX_LN_CASE(N) \
+  layernorm_fp32_kernel<IB, OB, N><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, w, ld_in, ld_out, eps)
+  if (nv <= 3) WX_LN_CASE(3);
+  else if (nv <= 4) WX_LN_CASE(4);
+  else if (nv <= 6) WX_LN_CASE(6);
+  else if (nv <= 8) WX_LN_CASE(8);
+  else if (nv <= 10) WX_LN_CASE(10);
+  else if (nv <= 16) WX_LN_CASE(16);
+  else WX_LN_CASE(0);
+#undef WX_LN_CASE
 }
 
 static int grid_for(int64_t work_items, int per_block, int blocks_per_sm) {
@@ -601,12 +663,13 @@ int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, cons
       (gamma && !aligned16(gamma)) || (beta && !aligned16(beta)))
     return fail(WX_ERR_INVALID, "layernorm fp32: cols and strides must be multiples of 4, "
                 "pointers 16-byte aligned");
-  const int grid = grid_for(rows, 8, 4);
+  const int grid = grid_for(rows, 8, 8);
   const bool ib = in_dtype == WX_DTYPE_BF16, ob = out_dtype == WX_DTYPE_BF16;
-  if (ib && ob) layernorm_fp32_kernel<true, true><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, (int)cols, ld_in, ld_out, eps);
-  else if (ib) layernorm_fp32_kernel<true, false><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, (int)cols, ld_in, ld_out, eps);
-  else if (ob) layernorm_fp32_kernel<false, true><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, (int)cols, ld_in, ld_out, eps);
-  else layernorm_fp32_kernel<false, false><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, (int)cols, ld_in, ld_out, eps);
+  const int w = (int)cols;
+  if (ib && ob) launch_ln_fp32<true, true>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps);
+  else if (ib) launch_ln_fp32<true, false>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps);
+  else if (ob) launch_ln_fp32<false, true>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps);
+  else launch_ln_fp32<false, false>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps);
   return check_launch("layernorm_fp32");
 }
 
