@@ -50,6 +50,16 @@ def test_gelu_every_bf16_value(cuda, mode):
     assert bits_equal(got, O.gelu_poly4(x, mode))
 
 
+@pytest.mark.parametrize("mode", [O.TRUNC, O.RNE])
+def test_gelu_infinities(cuda, mode):
+    """relu(x) + q with q = 0 past the last break: +inf -> +inf, -inf -> 0."""
+    x = np.array([[np.inf, -np.inf, 3.0e38, -3.0e38, 4.0, -4.0, 3.984375, -3.984375]],
+                 np.float32)
+    x = O.rbf(x, O.RNE)
+    got = host_f32(ops.gelu_poly4(bf16_dev(x), rounding=mode))
+    assert bits_equal(got, O.gelu_poly4(x, mode))
+
+
 @pytest.mark.parametrize("shape", [(1500, 1536), (1500, 5120), (7, 13), (3, 1000)])
 @pytest.mark.parametrize("mode", [O.TRUNC, O.RNE])
 def test_gelu_bf16_shapes(cuda, shape, mode):
@@ -139,6 +149,25 @@ def test_softmax_strided_rows(cuda):
     assert np.all(got[:, :16] == 0) and np.all(got[:, 176:] == 0)
 
 
+@pytest.mark.parametrize("variant,mode", [(4, O.RNE), (4, O.TRUNC), (1, O.RNE), (1, O.TRUNC)])
+@pytest.mark.parametrize("w", [1, 9, 200, 1500, 2041, 2048])
+def test_softmax_ragged_row_offsets(cuda, variant, mode, w):
+    """Rows starting at every 2-byte offset within 16 bytes, different offsets
+    for input and output, widths around the register-resident limit (2041)."""
+    rng = np.random.default_rng(w * 3 + variant)
+    rows = 37
+    x = O.rbf(rng.normal(0, 5, (rows, w)).astype(np.float32), O.RNE)
+    src = torch.zeros(rows, 2047 + 16, dtype=torch.bfloat16, device="cuda")
+    src[:, 3:3 + w] = bf16_dev(x)
+    dst = torch.full((rows, 2050 + 16), 7.0, dtype=torch.bfloat16, device="cuda")
+    ops.softmax_rows(src[:, 3:3 + w], out=dst[:, 5:5 + w], scale=0.5, variant=variant,
+                     rounding=mode)
+    got = host_f32(dst)
+    ref = O.softmax_row(x, mode=mode, variant=variant, scale=0.5)
+    assert bits_equal(got[:, 5:5 + w], ref)
+    assert np.all(got[:, :5] == 7.0) and np.all(got[:, 5 + w:] == 7.0)
+
+
 # ------------------------------------------------------------------ LayerNorm
 
 @pytest.mark.parametrize("mode", [O.TRUNC, O.RNE])
@@ -162,6 +191,26 @@ def test_layernorm_aie_gamma_beta(cuda, rows, cols):
                                        beta=torch.from_numpy(b).cuda(), mode=L.WX_LN_AIE,
                                        rounding=O.RNE))
     assert bits_equal(got, O.layer_norm_aie(x, O.RNE, gamma=g, beta=b))
+
+
+@pytest.mark.parametrize("mode", [O.TRUNC, O.RNE])
+@pytest.mark.parametrize("w", [1, 9, 200, 1280, 2041, 2048])
+def test_layernorm_aie_ragged_row_offsets(cuda, mode, w):
+    """Rows at every 2-byte offset within 16 bytes, input and output offsets
+    different, widths around the register-resident limit (2041), gamma/beta."""
+    rng = np.random.default_rng(w + 17)
+    rows = 29
+    x = O.rbf(rng.normal(0.2, 2.0, (rows, w)).astype(np.float32), O.RNE)
+    g = (1 + 0.1 * rng.standard_normal(w)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(w)).astype(np.float32)
+    src = torch.zeros(rows, 2047 + 16, dtype=torch.bfloat16, device="cuda")
+    src[:, 3:3 + w] = bf16_dev(x)
+    dst = torch.full((rows, 2050 + 16), 7.0, dtype=torch.bfloat16, device="cuda")
+    ops.layer_norm_rows(src[:, 3:3 + w], torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda(),
+                        out=dst[:, 5:5 + w], mode=L.WX_LN_AIE, rounding=mode)
+    got = host_f32(dst)
+    assert bits_equal(got[:, 5:5 + w], O.layer_norm_aie(x, mode, gamma=g, beta=b))
+    assert np.all(got[:, :5] == 7.0) and np.all(got[:, 5 + w:] == 7.0)
 
 
 @pytest.mark.parametrize("cols", [384, 1280, 4096])

@@ -78,22 +78,32 @@ __device__ __forceinline__ void rbf2(float& a, float& b) {
 
 // GELU-poly4 of two bf16 values (kernels/gelu_poly4_eval.inc:27-65). The
 // piece is selected, not branched on, so the compiler can interleave the
-// chains of many elements: with pa = [s < 1] and pb = [1 <= s < 2] as 0/1
-// floats, every coefficient is C2 + pa*(C0 - C2) + pb*(C1 - C2) by two FMAs
-// (the differences of bf16 coefficients are exact in fp32, so the selection is
-// exact), the shift 3 - 2.5*pa - 1.5*pb likewise, and the scale 1 + pa + pb is
-// 1 or 2, so u = R(s - shift) * scale needs no second rounding. This keeps the
-// selection on the FMA pipe (the ALU pipe carries the bf16 roundings); it was
-// checked on every bf16 input against the reference's evaluation order.
-// Elements past the last break keep q = 0 whatever their chain computed.
+// chains of many elements, and the selection runs on the FMA pipe (the ALU
+// pipe, at half its rate, carries the bf16 roundings):
+//  - the 0/1 indicators pa = [s < 1], [s < 2] and [s < 4] are saturating FMAs,
+//    sat(256 - 256 s) and so on: for bf16 s below a break the product is at
+//    least 1, at or above it at most 0 (NaN saturates to 0);
+//  - with pb = [s < 2] - pa, every coefficient is C2 + pa*(C0 - C2) +
+//    pb*(C1 - C2) by two FMAs (the differences of bf16 coefficients are exact
+//    in fp32), the shift 3 - 2.5*pa - 1.5*pb likewise, and the scale
+//    1 + pa + pb is 1 or 2, so u = R(s - shift) * scale needs no second
+//    rounding;
+//  - the chain runs on min(s, 4), which changes nothing where its value is
+//    kept and keeps it finite where it is multiplied by [s < 4] = 0.
+// Checked on every finite and infinite bf16 input, in both rounding modes,
+// against the reference's evaluation order.
 template <int R>
 __device__ __forceinline__ void gelu_poly4_x2(float& x0, float& x1) {
   constexpr float kC[3][5] = WX_GELU4_COEF;
   const float s0 = fabsf(x0), s1 = fabsf(x1);    // s = max(x, 0 - x)
-  const float pa0 = s0 < 1.0f ? 1.0f : 0.0f, pa1 = s1 < 1.0f ? 1.0f : 0.0f;
-  const float pb0 = (s0 < 2.0f ? 1.0f : 0.0f) - pa0, pb1 = (s1 < 2.0f ? 1.0f : 0.0f) - pa1;
-  float t0 = s0 - fmaf(pa0, -2.5f, fmaf(pb0, -1.5f, 3.0f));
-  float t1 = s1 - fmaf(pa1, -2.5f, fmaf(pb1, -1.5f, 3.0f));
+  const float pa0 = __saturatef(fmaf(s0, -256.0f, 256.0f));
+  const float pa1 = __saturatef(fmaf(s1, -256.0f, 256.0f));
+  const float pb0 = __saturatef(fmaf(s0, -128.0f, 256.0f)) - pa0;
+  const float pb1 = __saturatef(fmaf(s1, -128.0f, 256.0f)) - pa1;
+  const float in0 = __saturatef(fmaf(s0, -64.0f, 256.0f));
+  const float in1 = __saturatef(fmaf(s1, -64.0f, 256.0f));
+  float t0 = fminf(s0, 4.0f) - fmaf(pa0, -2.5f, fmaf(pb0, -1.5f, 3.0f));
+  float t1 = fminf(s1, 4.0f) - fmaf(pa1, -2.5f, fmaf(pb1, -1.5f, 3.0f));
   rbf2<R>(t0, t1);                                // bf16 sub
   const float u0 = t0 * (1.0f + pa0 + pb0), u1 = t1 * (1.0f + pa1 + pb1);  // exact
   auto coef = [&](int k, float pa, float pb) {
@@ -107,8 +117,8 @@ __device__ __forceinline__ void gelu_poly4_x2(float& x0, float& x1) {
     acc1 = fmaf(acc1, u1, coef(k, pa1, pb1));
   }
   rbf2<R>(acc0, acc1);
-  float r0 = ((x0 >= 0.0f) ? x0 : 0.0f) + (s0 < 4.0f ? acc0 : 0.0f);   // relu(x) + q
-  float r1 = ((x1 >= 0.0f) ? x1 : 0.0f) + (s1 < 4.0f ? acc1 : 0.0f);
+  float r0 = fmaxf(x0, 0.0f) + acc0 * in0;        // relu(x) + q
+  float r1 = fmaxf(x1, 0.0f) + acc1 * in1;
   rbf2<R>(r0, r1);
   x0 = r0;
   x1 = r1;
@@ -315,6 +325,29 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
 __device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo_bytes) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// The same descriptors as two 32-bit words. The high word (stride byte offset
+// 1024, version 1, SWIZZLE_128B) is a constant of the layout; the low word is
+// the start address >> 4 with the leading byte offset, so stepping along K (32
+// bytes: +2) or between ring slots is one 32-bit add in the MMA issuer's loop.
+constexpr uint32_t kSdescHiSw128 = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t sdesc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+// D[tmem] (+)= A[smem] * B[smem]^T with the descriptors given as low words
+// (shared high word `hi`).
+__device__ __forceinline__ void umma_bf16_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                                uint32_t hi, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "mov.b64 ad, {%1, %5};\n\t"
+      "mov.b64 bd, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(hi)
+      : "memory");
 }
 
 // Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), bf16 A

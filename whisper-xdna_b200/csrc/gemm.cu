@@ -213,6 +213,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_bf16_f32(kGemmBM, BN, 0, 0);
+      const uint32_t hi = kSdescHiSw128;
+      const uint32_t a_lo = sdesc_lo(smem_u32(sA), 16), b_lo = sdesc_lo(smem_u32(sB), 16);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -223,12 +225,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < nkb; kb++) {
           if (!mbar_wait(&full[stage], phase, a.err)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * Cfg::A_BYTES);
-          const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
+          const uint32_t ad = a_lo + (uint32_t)(stage * (Cfg::A_BYTES >> 4));
+          const uint32_t bd = b_lo + (uint32_t)(stage * (Cfg::B_BYTES >> 4));
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; k++)
-            umma_bf16_ss(d_tmem, sdesc_kmajor_sw128(a_base + k * 32),
-                         sdesc_kmajor_sw128(b_base + k * 32), idesc, (kb | k) != 0);
+          for (int k = 0; k < kGemmBK / 16; k++)   // 32 bytes of K per MMA: +2
+            umma_bf16_ss_lo(d_tmem, ad + 2 * k, bd + 2 * k, hi, idesc, (kb | k) != 0);
           umma_commit(&empty[stage]);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }

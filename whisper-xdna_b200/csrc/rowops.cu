@@ -12,6 +12,7 @@
 //   LN       kernels/layer_norm_gb.cc:22-85
 // Memory access: 16-byte vector loads and stores, rows staged in shared memory
 // so HBM is read and written once.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -109,17 +110,18 @@ static int exp_tables(ExpTablesDev** out) {
 }
 
 // ---------------------------------------------------------------- GELU
+// Rows are strided over blockIdx.y, VEC-element column groups over
+// blockIdx.x and the threads, so no thread divides an index.
 template <int R, bool F32IN, int VEC>
-__global__ void __launch_bounds__(256) gelu_poly4_kernel(const void* __restrict__ in,
+__global__ void __launch_bounds__(128) gelu_poly4_kernel(const void* __restrict__ in,
                                                          uint16_t* __restrict__ out,
                                                          int64_t rows, int64_t cols,
                                                          int64_t ld_in, int64_t ld_out) {
   const int64_t per_row = cols / VEC;
-  const int64_t total = rows * per_row;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per_row;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / per_row;
-    const int64_t c = (i - r * per_row) * VEC;
+    const int64_t c = i * VEC;
     float x[VEC];
     if (F32IN) {
       const float* src = reinterpret_cast<const float*>(in) + r * ld_in + c;
@@ -365,6 +367,161 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(
   }
 }
 
+// The v1 / v4 forms for windows of up to 256 * NV - 7 columns: each warp holds
+// its row in registers as NV 16-byte chunks per lane (chunk v = lane + 32k),
+// read from the row start rounded down to 16 bytes, so any bf16 row layout
+// (e.g. 1500 columns, rows alternately 0 and 8 bytes off a 16-byte boundary)
+// reads and writes HBM once with 16-byte accesses; elements outside the
+// window in the edge chunks are masked to -inf and never written. The
+// exponentials go to shared memory in that chunk layout for the 16-lane
+// summation and are read back from there for the output. Values stay packed
+// as bf16 pairs: the max is a bf16x2 max (exact), x' - max in RNE mode a
+// bf16x2 subtraction, whose correctly rounded result equals the fp32
+// difference rounded to bf16 (fp32 carries more than 2 * 8 + 2 significand
+// bits, so the double rounding is innocuous). The exponential is the bf16
+// table in shared memory, indexed without branches: x' <= max, so d <= 0 and
+// its magnitude bits are the table index; d <= -128, and NaN, clamp to a
+// trailing zero entry.
+constexpr int kSmRegThreads = 512;
+constexpr int kExpTabBytes = ((kExpTabN + 1) * 2 + 15) / 16 * 16;
+
+__device__ __forceinline__ int chunk_head(const void* p) {
+  return (int)((reinterpret_cast<uintptr_t>(p) & 15) >> 1);
+}
+
+template <int R, int VAR, int NV>
+__global__ void __launch_bounds__(kSmRegThreads, 2) softmax_rows_reg_kernel(
+    const uint16_t* __restrict__ in, uint16_t* __restrict__ out, int64_t rows, int w,
+    int64_t ld_in, int64_t ld_out, float scale, const uint16_t* __restrict__ t16_g) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  for (int i = threadIdx.x; i < kExpTabN / 8; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = __ldg(reinterpret_cast<const uint4*>(t16_g) + i);
+  if (threadIdx.x == 0) reinterpret_cast<uint16_t*>(smem)[kExpTabN] = 0;
+  __syncthreads();
+  const uint8_t* tab = smem;
+  const int warps = blockDim.x >> 5, warp = warp_id(), lane = lane_id();
+  uint4* buf = reinterpret_cast<uint4*>(smem + kExpTabBytes) + (size_t)warp * (NV * 32);
+  const uint16_t* buf16 = reinterpret_cast<const uint16_t*>(buf);
+  const bool do_scale = scale != 1.0f;
+  for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
+       row += (int64_t)gridDim.x * warps) {
+    const uint16_t* src_row = in + row * ld_in;
+    const int h = chunk_head(src_row);  // elements before column 0 in chunk 0
+    const int nch = (w + h + 7) >> 3;
+    const uint4* src = reinterpret_cast<const uint4*>(src_row - h);
+    uint32_t x[NV * 4];
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      uint4 q = make_uint4(0u, 0u, 0u, 0u);
+      if (lane + 32 * k < nch) q = __ldg(src + lane + 32 * k);
+      x[4 * k] = q.x; x[4 * k + 1] = q.y; x[4 * k + 2] = q.z; x[4 * k + 3] = q.w;
+    }
+    // x' = R(x * scale); elements outside [0, w) become -inf
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int c0 = 8 * (lane + 32 * k) - h;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        uint32_t& v = x[4 * k + j];
+        if (do_scale)
+          v = pack_bf16x2<R>(__fmul_rn(__uint_as_float(v << 16), scale),
+                             __fmul_rn(__uint_as_float(v & 0xFFFF0000u), scale));
+        if (c0 < 0 || c0 + 8 > w) {
+          const int c = c0 + 2 * j;
+          if (c < 0 || c >= w) v = (v & 0xFFFF0000u) | 0xFF80u;
+          if (c + 1 < 0 || c + 1 >= w) v = (v & 0xFFFFu) | 0xFF800000u;
+        }
+      }
+    }
+    // row max seeded with (bfloat16)-30000 (softmax_row4_body.inc:22-28)
+    __nv_bfloat162 mx = *reinterpret_cast<const __nv_bfloat162*>(&x[0]);
+#pragma unroll
+    for (int i = 1; i < NV * 4; i++)
+      mx = __hmax2(mx, *reinterpret_cast<const __nv_bfloat162*>(&x[i]));
+    const float m = fmaxf(warp_max(fmaxf(__low2float(mx), __high2float(mx))), -29952.0f);
+    const __nv_bfloat162 m2 = __float2bfloat162_rn(m);
+    // e = R(exp(R(x' - m))), in place of x'
+#pragma unroll
+    for (int i = 0; i < NV * 4; i++) {
+      uint32_t d;
+      if (R == RND_RNE) {
+        const __nv_bfloat162 t = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&x[i]), m2);
+        d = *reinterpret_cast<const uint32_t*>(&t);
+      } else {
+        d = pack_bf16x2<R>(__fsub_rn(__uint_as_float(x[i] << 16), m),
+                           __fsub_rn(__uint_as_float(x[i] & 0xFFFF0000u), m));
+      }
+      const uint32_t off = (d << 1) & 0xFFFEFFFEu;  // magnitude * 2 in each half
+      const uint32_t olo = min(off & 0xFFFFu, (uint32_t)(2 * kExpTabN));
+      const uint32_t ohi = min(off >> 16, (uint32_t)(2 * kExpTabN));
+      x[i] = (uint32_t)*reinterpret_cast<const uint16_t*>(tab + olo) |
+             ((uint32_t)*reinterpret_cast<const uint16_t*>(tab + ohi) << 16);
+    }
+#pragma unroll
+    for (int k = 0; k < NV; k++)
+      buf[lane + 32 * k] = make_uint4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
+    __syncwarp();
+    // 16 fp32 lanes, lane l summing e over columns l, l+16, ... (softmax_row4_body.inc:31-40)
+    float acc = 0.0f;
+    if (lane < 16) {
+#pragma unroll 8
+      for (int c = lane; c < w; c += 16) acc = __fadd_rn(acc, bits_f32(buf16[c + h]));
+    }
+    const float sum = __shfl_sync(0xffffffffu, lane16_tree(acc), 0);
+    const float inv = __fdiv_rn(1.0f, sum);                 // aie::inv
+    const float ihi = rbf<R>(inv);                          // softmax_row4_body.inc:45-46
+    const float ilo = rbf<R>(__fsub_rn(inv, ihi));
+    // p = R(e*hi + e*lo) (softmax_row4_body.inc:51-60); v1 is R(e*hi)
+    // (softmax_row.cc:50-57). The products are kept as separate roundings: they
+    // are exact except in the subnormal range, where an fma could differ.
+    uint16_t* dst_row = out + row * ld_out;
+    const int ho = chunk_head(dst_row);
+    const int ncho = (w + ho + 7) >> 3;
+    uint4* dst = reinterpret_cast<uint4*>(dst_row - ho);
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int u = lane + 32 * k;
+      if (u < ncho) {
+        const int c0 = 8 * u - ho;
+        uint32_t e[4];
+        if (ho == h) {
+          const uint4 q = buf[u];
+          e[0] = q.x; e[1] = q.y; e[2] = q.z; e[3] = q.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int c = c0 + 2 * j;
+            const uint32_t lo = (c >= 0 && c < w) ? buf16[c + h] : 0u;
+            const uint32_t hi = (c + 1 >= 0 && c + 1 < w) ? buf16[c + 1 + h] : 0u;
+            e[j] = lo | (hi << 16);
+          }
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float elo = __uint_as_float(e[j] << 16);
+          const float ehi = __uint_as_float(e[j] & 0xFFFF0000u);
+          if (VAR == 1)
+            o[j] = pack_bf16x2<R>(__fmul_rn(elo, ihi), __fmul_rn(ehi, ihi));
+          else
+            o[j] = pack_bf16x2<R>(__fadd_rn(__fmul_rn(elo, ihi), __fmul_rn(elo, ilo)),
+                                  __fadd_rn(__fmul_rn(ehi, ihi), __fmul_rn(ehi, ilo)));
+        }
+        if (c0 >= 0 && c0 + 8 <= w) {
+          dst[u] = make_uint4(o[0], o[1], o[2], o[3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            const int c = c0 + j;
+            if (c >= 0 && c < w) dst_row[c] = (uint16_t)(o[j >> 1] >> (16 * (j & 1)));
+          }
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
 // ---------------------------------------------------------------- LayerNorm
 // kernels/layer_norm_gb.cc:22-34, every fp32 operation rounded on its own.
 __device__ __forceinline__ float rsqrt_nr(float x) {
@@ -431,6 +588,99 @@ __global__ void __launch_bounds__(256) layernorm_aie_kernel(
       done = nv * 8;
     }
     for (int c = done + lane; c < w; c += 32) dst[c] = (uint16_t)bf16_bits<R>(norm(bits_f32(buf[c]), c));
+    __syncwarp();
+  }
+}
+
+// The same arithmetic for rows of up to 256 * NV - 7 columns, read as 16-byte
+// chunks from the row start rounded down to 16 bytes (the
+// softmax_rows_reg_kernel layout) with all of a row's loads in flight
+// together, then kept in shared memory for the 16-lane sums and the
+// normalisation; gamma / beta are staged in shared memory once per CTA.
+template <int R, int NV>
+__global__ void __launch_bounds__(256) layernorm_aie_reg_kernel(
+    const uint16_t* __restrict__ in, const float* __restrict__ gamma,
+    const float* __restrict__ beta, uint16_t* __restrict__ out, int64_t rows, int w,
+    int64_t ld_in, int64_t ld_out, float eps) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int warps = blockDim.x >> 5, warp = warp_id(), lane = lane_id();
+  const bool affine = gamma != nullptr || beta != nullptr;
+  float* g_s = reinterpret_cast<float*>(smem);             // [w] gamma, then [w] beta
+  float* b_s = g_s + w;
+  uint4* buf = reinterpret_cast<uint4*>(smem + (((size_t)2 * w * 4 + 15) & ~(size_t)15)) +
+               (size_t)warp * (NV * 32);
+  const uint16_t* buf16 = reinterpret_cast<const uint16_t*>(buf);
+  if (affine) {
+    for (int c = threadIdx.x; c < w; c += blockDim.x) {
+      g_s[c] = gamma ? gamma[c] : 1.0f;
+      b_s[c] = beta ? beta[c] : 0.0f;
+    }
+  }
+  __syncthreads();
+  const float inv_n = __fdiv_rn(1.0f, (float)w);                          // :69
+  for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
+       row += (int64_t)gridDim.x * warps) {
+    const uint16_t* src_row = in + row * ld_in;
+    const int h = chunk_head(src_row);
+    const int nch = (w + h + 7) >> 3;
+    const uint4* src = reinterpret_cast<const uint4*>(src_row - h);
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      uint4 q = make_uint4(0u, 0u, 0u, 0u);
+      if (lane + 32 * k < nch) q = __ldg(src + lane + 32 * k);
+      buf[lane + 32 * k] = q;
+    }
+    __syncwarp();
+    // pass 1 (:61-67): sum and sum of squares in 16 fp32 lanes
+    float s1 = 0.0f, s2 = 0.0f;
+    if (lane < 16) {
+#pragma unroll 4
+      for (int c = lane; c < w; c += 16) {
+        const float x = bits_f32(buf16[c + h]);
+        s1 = __fadd_rn(s1, x);
+        s2 = __fadd_rn(s2, __fmul_rn(x, x));
+      }
+    }
+    s1 = __shfl_sync(0xffffffffu, lane16_tree(s1), 0);
+    s2 = __shfl_sync(0xffffffffu, lane16_tree(s2), 0);
+    const float mean = __fmul_rn(s1, inv_n);                             // :70
+    const float var = __fsub_rn(__fmul_rn(s2, inv_n), __fmul_rn(mean, mean));  // :71
+    const float inv = rsqrt_nr(__fadd_rn(var, eps));                     // :72
+    const float mb = rbf<R>(mean), ib = rbf<R>(inv);                     // :74-77
+    auto norm = [&](float x, int c) -> float {                           // :80-85
+      float o = rbf<R>(__fmul_rn(rbf<R>(__fsub_rn(x, mb)), ib));
+      if (affine) o = rbf<R>(__fadd_rn(__fmul_rn(o, g_s[c]), b_s[c]));
+      return o;
+    };
+    uint16_t* dst_row = out + row * ld_out;
+    const int ho = chunk_head(dst_row);
+    const int ncho = (w + ho + 7) >> 3;
+    uint4* dst = reinterpret_cast<uint4*>(dst_row - ho);
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int u = lane + 32 * k;
+      if (u < ncho) {
+        const int c0 = 8 * u - ho;
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int c = c0 + 2 * j;
+          const bool in0 = c >= 0 && c < w, in1 = c + 1 >= 0 && c + 1 < w;
+          const float x0 = in0 ? bits_f32(buf16[c + h]) : 0.0f;
+          const float x1 = in1 ? bits_f32(buf16[c + 1 + h]) : 0.0f;
+          o[j] = pack_bf16x2<R>(norm(x0, in0 ? c : 0), norm(x1, in1 ? c + 1 : 0));
+        }
+        if (c0 >= 0 && c0 + 8 <= w) {
+          dst[u] = make_uint4(o[0], o[1], o[2], o[3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            const int c = c0 + j;
+            if (c >= 0 && c < w) dst_row[c] = (uint16_t)(o[j >> 1] >> (16 * (j & 1)));
+          }
+        }
+      }
+    }
     __syncwarp();
   }
 }
@@ -560,11 +810,13 @@ int launch_gelu_poly4(const void* in, int in_dtype, void* out, int64_t rows, int
   const bool f32 = in_dtype == WX_DTYPE_F32;
   const bool vec = cols % 8 == 0 && ld_in % 8 == 0 && ld_out % 8 == 0 && aligned16(in) &&
                    aligned16(out);
-  const int64_t items = rows * (vec ? cols / 8 : cols);
-  const int grid = grid_for(items, 256, 8);
+  const int64_t per_row = vec ? cols / 8 : cols;
+  const int gx = (int)std::min<int64_t>((per_row + 127) / 128, 64);
+  const int64_t want_y = ((int64_t)sm_count() * 16 + gx - 1) / gx;
+  const dim3 grid(gx, (unsigned)std::min<int64_t>(std::min<int64_t>(rows, want_y), 65535));
   uint16_t* o = reinterpret_cast<uint16_t*>(out);
 #define WX_GELU_LAUNCH(R, F, V) \
-  gelu_poly4_kernel<R, F, V><<<grid, 256, 0, st>>>(in, o, rows, cols, ld_in, ld_out)
+  gelu_poly4_kernel<R, F, V><<<grid, 128, 0, st>>>(in, o, rows, cols, ld_in, ld_out)
   if (rounding == RND_RNE) {
     if (f32) { if (vec) WX_GELU_LAUNCH(RND_RNE, true, 8); else WX_GELU_LAUNCH(RND_RNE, true, 1); }
     else { if (vec) WX_GELU_LAUNCH(RND_RNE, false, 8); else WX_GELU_LAUNCH(RND_RNE, false, 1); }
@@ -601,6 +853,40 @@ int launch_softmax_rows(const void* in, void* out, int64_t rows, int64_t cols, i
     return fail(WX_ERR_INVALID, "softmax: rounding %d", rounding);
   ExpTablesDev* tabs = nullptr;
   WX_TRY(exp_tables(&tabs));
+  const uint16_t* i16 = reinterpret_cast<const uint16_t*>(in);
+  uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+  const bool even = (reinterpret_cast<uintptr_t>(in) & 1) == 0 &&
+                    (reinterpret_cast<uintptr_t>(out) & 1) == 0;
+  if (variant != 3 && even && w <= 8 * 32 * 8 - 7) {
+    const int chunks = (int)(((w + 7 + 7) / 8 + 31) / 32);
+    const int nvc = chunks <= 2 ? chunks : chunks <= 4 ? 4 : chunks <= 6 ? 6 : 8;
+    const int wps = kSmRegThreads / 32;
+    const size_t smem = kExpTabBytes + (size_t)wps * nvc * 32 * 16;
+    const int grid = grid_for(rows, wps, 2);
+#define WX_SMR_LAUNCH(R, V, N)                                                                \
+  do {                                                                                        \
+    auto k = softmax_rows_reg_kernel<R, V, N>;                                                \
+    WX_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+    k<<<grid, kSmRegThreads, smem, st>>>(i16, o16, rows, (int)w, ld_in, ld_out, scale,       \
+                                         tabs->t16[R]);                                      \
+  } while (0)
+#define WX_SMR_NV(R, V)                       \
+  do {                                        \
+    if (nvc == 1) WX_SMR_LAUNCH(R, V, 1);     \
+    else if (nvc == 2) WX_SMR_LAUNCH(R, V, 2); \
+    else if (nvc == 4) WX_SMR_LAUNCH(R, V, 4); \
+    else if (nvc == 6) WX_SMR_LAUNCH(R, V, 6); \
+    else WX_SMR_LAUNCH(R, V, 8);              \
+  } while (0)
+    if (rounding == RND_RNE) {
+      if (variant == 4) WX_SMR_NV(RND_RNE, 4); else WX_SMR_NV(RND_RNE, 1);
+    } else {
+      if (variant == 4) WX_SMR_NV(RND_TRUNC, 4); else WX_SMR_NV(RND_TRUNC, 1);
+    }
+#undef WX_SMR_NV
+#undef WX_SMR_LAUNCH
+    return check_launch("softmax_rows");
+  }
   const int wpad = (int)((w + 7) / 8 * 8);
   const size_t fixed = ((kExpTabN * 2 + 15) / 16) * 16 + (variant == 3 ? kExpTabN * 4 : 0);
   const int wps = row_warps(fixed, (size_t)wpad * 2);
@@ -608,8 +894,6 @@ int launch_softmax_rows(const void* in, void* out, int64_t rows, int64_t cols, i
   const int vin = (w % 8 == 0 && ld_in % 8 == 0 && aligned16(in)) ? 1 : 0;
   const int vout = (w % 8 == 0 && ld_out % 8 == 0 && aligned16(out)) ? 1 : 0;
   const int grid = grid_for(rows, wps, 2);
-  const uint16_t* i16 = reinterpret_cast<const uint16_t*>(in);
-  uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
 #define WX_SM_LAUNCH(R, V)                                                                   \
   do {                                                                                       \
     auto k = softmax_rows_kernel<R, V>;                                                      \
@@ -639,6 +923,35 @@ int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, cons
     if (rounding != RND_TRUNC && rounding != RND_RNE)
       return fail(WX_ERR_INVALID, "layernorm: rounding %d", rounding);
     if (cols > 65536) return fail(WX_ERR_UNSUPPORTED, "layernorm: cols %lld > 65536", (long long)cols);
+    const bool even = (reinterpret_cast<uintptr_t>(in) & 1) == 0 &&
+                      (reinterpret_cast<uintptr_t>(out) & 1) == 0;
+    if (even && cols <= 8 * 32 * 8 - 7) {
+      const int w = (int)cols;
+      const int chunks = (w + 14) / 8;
+      const int nvc = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 192 ? 6 : 8;
+      const size_t smem = (((size_t)2 * w * 4 + 15) & ~(size_t)15) + (size_t)8 * nvc * 32 * 16;
+      const int grid = grid_for(rows, 8, 8);
+      const uint16_t* i16 = reinterpret_cast<const uint16_t*>(in);
+      uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
+#define WX_LNR_LAUNCH(R, N)                                                                   \
+  do {                                                                                        \
+    auto k = layernorm_aie_reg_kernel<R, N>;                                                  \
+    WX_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+    k<<<grid, 256, smem, st>>>(i16, gamma, beta, o16, rows, w, ld_in, ld_out, eps);           \
+  } while (0)
+#define WX_LNR_NV(R)                           \
+  do {                                         \
+    if (nvc == 1) WX_LNR_LAUNCH(R, 1);         \
+    else if (nvc == 2) WX_LNR_LAUNCH(R, 2);    \
+    else if (nvc == 4) WX_LNR_LAUNCH(R, 4);    \
+    else if (nvc == 6) WX_LNR_LAUNCH(R, 6);    \
+    else WX_LNR_LAUNCH(R, 8);                  \
+  } while (0)
+      if (rounding == RND_RNE) WX_LNR_NV(RND_RNE); else WX_LNR_NV(RND_TRUNC);
+#undef WX_LNR_NV
+#undef WX_LNR_LAUNCH
+      return check_launch("layernorm_aie");
+    }
     const int wpad = (int)((cols + 7) / 8 * 8);
     const int wps = row_warps(0, (size_t)wpad * 2);
     const size_t smem = (size_t)wps * wpad * 2;

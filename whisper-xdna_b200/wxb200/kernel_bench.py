@@ -79,21 +79,27 @@ def setup(kernel, batch, dev="cuda"):
 
 def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False):
     fn, flop, byt = setup(kernel, batch)
-    junk = torch.empty(256 * 1024 * 1024 // 4, device="cuda") if flush else None
+    # 1 GiB: its fill (~160 us) outlasts the host-side cost of one launch
+    junk = torch.empty(1024 * 1024 * 1024 // 4, device="cuda") if flush else None
     st = torch.cuda.current_stream()
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     total = 0.0
     if flush:
+        # Everything is enqueued before one synchronize: while the GPU writes
+        # the flush buffer the host has already queued the timed launch, so
+        # the event pair brackets the kernel, not the host's launch overhead.
+        evs = []
         for _ in range(iters):
             junk.fill_(1.0)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
             fn()
             e1.record(st)
-            torch.cuda.synchronize()
-            total += e0.elapsed_time(e1) / 1e3
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        total = sum(a.elapsed_time(b) for a, b in evs) / 1e3
     else:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
