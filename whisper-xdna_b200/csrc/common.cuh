@@ -124,11 +124,59 @@ __device__ __forceinline__ void gelu_poly4_x2(float& x0, float& x1) {
   x1 = r1;
 }
 
+// The same function in RNE mode on two bf16 values packed in a word, with
+// bf16x2 arithmetic: every bf16x2 operation rounds its exact result once, and
+// on every finite bf16 input this reproduces the reference's fp32-then-bf16
+// steps bit for bit (checked exhaustively against the CPU restatement, and on
+// the GPU by the every-input test). The indicators are bf16x2 compares
+// (1.0 / 0.0), each coefficient is pa*C0 + pb*C1 + pc*C2 with exactly one term
+// nonzero (exact), and relu(x) + q is one fma with q = acc * [s < 4].
+// About 33 instructions per pair instead of about 76 for the fp32 form.
+// Coefficient bit patterns: the bf16 values of WX_GELU4_COEF.
+#define WX_GELU4_COEF_BITS                                  \
+  {{0xBB06u, 0xBC55u, 0x3D9Eu, 0xBD88u, 0xBE1Eu},            \
+   {0x3B0Du, 0xBBEBu, 0xBB84u, 0x3D83u, 0xBDCDu},            \
+   {0xBB40u, 0x3C2Fu, 0xBC82u, 0x3C45u, 0xBB84u}}
+__device__ __forceinline__ __nv_bfloat162 bf2_bits(uint32_t w) {
+  return *reinterpret_cast<const __nv_bfloat162*>(&w);
+}
+__device__ __forceinline__ __nv_bfloat162 bf2_splat(uint32_t h) { return bf2_bits(h | (h << 16)); }
+__device__ __forceinline__ uint32_t gelu_poly4_bf16x2_rne(uint32_t xw) {
+  constexpr uint32_t kCb[3][5] = WX_GELU4_COEF_BITS;
+  const __nv_bfloat162 x = bf2_bits(xw);
+  const __nv_bfloat162 s = bf2_bits(xw & 0x7FFF7FFFu);      // |x|
+  const __nv_bfloat162 one = bf2_splat(0x3F80u), four = bf2_splat(0x4080u);
+  const __nv_bfloat162 pa = __hlt2(s, one);                  // [s < 1]
+  const __nv_bfloat162 pab = __hlt2(s, bf2_splat(0x4000u));  // [s < 2]
+  const __nv_bfloat162 in4 = __hlt2(s, four);                // [s < 4]
+  const __nv_bfloat162 pb = __hsub2(pab, pa), pc = __hsub2(one, pab);
+  const __nv_bfloat162 shift =
+      __hfma2(pa, bf2_splat(0xC020u), __hfma2(pb, bf2_splat(0xBFC0u), bf2_splat(0x4040u)));
+  const __nv_bfloat162 t = __hsub2(__hmin2(s, four), shift);    // bf16 sub
+  const __nv_bfloat162 u = __hmul2(t, __hadd2(one, pab));        // exact (x1 or x2)
+  auto coef = [&](int k) {
+    return __hfma2(pa, bf2_splat(kCb[0][k]),
+                   __hfma2(pb, bf2_splat(kCb[1][k]), __hmul2(pc, bf2_splat(kCb[2][k]))));
+  };
+  __nv_bfloat162 acc = coef(0);
+#pragma unroll
+  for (int k = 1; k < 5; k++) acc = __hfma2(acc, u, coef(k));   // Horner
+  const __nv_bfloat162 r = __hfma2(acc, in4, __hmax2(x, bf2_splat(0u)));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
 template <int R>
 __device__ __forceinline__ float gelu_poly4(float x) {
   float y = 0.0f;
   gelu_poly4_x2<R>(x, y);
   return x;
+}
+
+// max of three floats in one instruction (sm_100 three-input max.f32).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // 2^x on the SFU (MUFU.EX2), flushing denormal results; 2^-inf = +0.

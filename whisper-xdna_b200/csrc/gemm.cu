@@ -81,10 +81,29 @@ __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int row, int
     }
   }
   if (EPI == WX_EPI_BF16_GELU || EPI == kEpiF32GeluPos) {
+    // g4f: input rounded to bf16 (RNE), then poly4 on packed pairs
+    uint32_t w[16];
 #pragma unroll
-    for (int j = 0; j < 32; j += 2) {  // g4f: input rounded to bf16 (RNE), then poly4
-      rbf2<RND_RNE>(v[j], v[j + 1]);
-      gelu_poly4_x2<RND_RNE>(v[j], v[j + 1]);
+    for (int j = 0; j < 16; j++)
+      w[j] = gelu_poly4_bf16x2_rne(pack_bf16x2_rne(v[2 * j], v[2 * j + 1]));
+    if constexpr (EPI == WX_EPI_BF16_GELU) {
+      uint16_t* c = reinterpret_cast<uint16_t*>(a.C) + (int64_t)row * a.ldc + n;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<uint4*>(c + 2 * j) = make_uint4(w[j], w[j + 1], w[j + 2], w[j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (n + j < a.N) c[j] = (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
+      }
+      return;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        v[2 * j] = __uint_as_float(w[j] << 16);
+        v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+      }
     }
   }
   if (EPI == WX_EPI_BF16_GELU_ERF || EPI == kEpiF32GeluErfPos) {

@@ -150,7 +150,13 @@ __global__ void __launch_bounds__(128) gelu_poly4_kernel(const void* __restrict_
       }
     }
     uint16_t* dst = out + r * ld_out + c;
-    if (VEC == 8) {
+    if (VEC == 8 && R == RND_RNE) {   // packed bf16x2 form
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        w[j] = gelu_poly4_bf16x2_rne(pack_bf16x2_rne(x[2 * j], x[2 * j + 1]));
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else if (VEC == 8) {
 #pragma unroll
       for (int j = 0; j < 8; j += 2) gelu_poly4_x2<R>(x[j], x[j + 1]);
       uint4 o;
