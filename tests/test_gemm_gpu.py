@@ -44,6 +44,37 @@ SHAPES = [
 ]
 
 
+# Shapes large enough for the 2-SM kernel (CTA pairs, 256 x 256 tiles: at
+# least 74 pair tiles), with M, N and K off every tile boundary.
+PAIR_SHAPES = [(5000, 1000, 1000), (4100, 1288, 1336), (19000, 256, 64), (1500, 5120, 1280)]
+
+
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+@pytest.mark.parametrize("epi", ["f32", "bf16", "resid", "gelu"])
+def test_gemm_pair_kernel_epilogues(cuda, M, N, K, epi):
+    A, W = rand_bf16((M, K), M + 3), rand_bf16((N, K), N + 5, 0.05)
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(K)).cuda() * 0.1
+    if epi == "f32":
+        got = ops.gemm(A, W, bias=bias, epilogue=L.WX_EPI_F32)
+        ref = ref_mm(A, W, bias)
+        assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-5
+    elif epi == "bf16":
+        got = ops.gemm(A, W, bias=bias, epilogue=L.WX_EPI_BF16).float()
+        ref = ref_mm(A, W, bias)
+        assert ((got - ref).abs() <= ref.abs() * 2 ** -8 + 1e-3 * ref.abs().max()).all()
+    elif epi == "resid":
+        x = torch.randn(M, N, generator=torch.Generator().manual_seed(M)).cuda()
+        ref = ref_mm(A, W, bias, x)
+        ops.gemm(A, W, bias=bias, residual=x, out=x, epilogue=L.WX_EPI_F32_RESID)
+        assert (x - ref).abs().max().item() / ref.abs().max().item() < 1e-5
+    else:
+        acc = ops.gemm(A, W, bias=bias, epilogue=L.WX_EPI_F32)
+        got = ops.gemm(A, W, bias=bias, epilogue=L.WX_EPI_BF16_GELU)
+        g = (got.cpu().view(torch.int16).numpy().view(np.uint16).astype(np.uint32) << 16)
+        assert np.array_equal(g.view(np.float32), O.gelu_row4f(acc.cpu().numpy()))
+    assert L.device_error() == 0
+
+
 @pytest.mark.parametrize("M,N,K", SHAPES)
 def test_gemm_f32_bias(cuda, M, N, K):
     A, W = rand_bf16((M, K), M + K), rand_bf16((N, K), N + 1, 0.05)

@@ -22,6 +22,8 @@
 // RawRT.matmul / mm_start / mm_finish (src/rawxrt.py:926-996); its bias fold
 // (ones column on A, bias row on B, src/rawxrt.py:352-371) becomes a bias
 // added to the fp32 accumulator in the epilogue.
+#include <algorithm>
+
 #include "common.cuh"
 #include "plans.cuh"
 
@@ -309,7 +311,254 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-static int gemm_prepare(int bn, int epi);
+// ---------------------------------------------------------------- 2-SM GEMM
+// The same GEMM on CTA pairs (a cluster of two, tcgen05 cta_group::2): the
+// pair computes 256 x 256 tiles with M=256, N=256 MMAs issued by the leader
+// (cluster rank 0). Rank r stages rows [128 r, 128 r + 128) of the A tile and
+// rows [128 r, 128 r + 128) of the B tile (32 KB per 64-wide K step instead
+// of 48 KB for 128 x 256 on one SM, so six stages fit), and holds accumulator
+// rows [128 r, 128 r + 128) x 256 columns in its own tensor memory; the
+// tensor cores of the pair exchange the B halves themselves. Synchronisation:
+//   full[s]    leader only: armed by the leader's producer with both CTAs'
+//              bytes; both CTAs' TMA loads complete on it (cta_group::2 form)
+//   empty[s]   both CTAs: the leader commits the MMAs of a step to its own
+//              and to the peer's barrier (two commits, same offset)
+//   tfull[b]   both CTAs, committed like empty
+//   tempty[b]  leader only: one arrival per epilogue warp of either CTA
+// Every wait is bounded; both CTAs always reach the final cluster barrier,
+// after which the tensor memory of the pair is released.
+constexpr int kGemm2Stages = 6;
+constexpr int kGemm2ABytes = 128 * kGemmBK * 2;                   // 16 KB
+constexpr int kGemm2BBytes = 128 * kGemmBK * 2;                   // 16 KB (half of N=256)
+constexpr int kGemm2StageBytes = kGemm2ABytes + kGemm2BBytes;
+constexpr int kGemm2Smem = kGemm2Stages * kGemm2StageBytes + 1024 + 256;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the variable at local shared address `a` in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// TMA tile load into this CTA's shared memory, completing on an mbarrier that
+// may be the peer CTA's (cta_group::2 form; not a multicast)
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster,
+                                                 void* dst, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx_local(uint64_t* bar, uint32_t bytes) {
+  mbar_arrive_expect_tx(bar, bytes);
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+__device__ __forceinline__ void umma_bf16_ss_lo_pair(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                                     uint32_t hi, uint32_t idesc,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "mov.b64 ad, {%1, %5};\n\t"
+      "mov.b64 bd, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], ad, bd, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(hi)
+      : "memory");
+}
+// Arrive on the mbarrier at shared::cluster address `bar` (either CTA of the
+// pair) once every cta_group::2 MMA issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+  constexpr int S = kGemm2Stages;
+  constexpr int BN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * kGemm2ABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kGemm2StageBytes);
+  uint64_t* full = bars;            // [S], used in the leader
+  uint64_t* empty = bars + S;       // [S]
+  uint64_t* tfull = bars + 2 * S;   // [2]
+  uint64_t* tempty = tfull + 2;     // [2], used in the leader
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * (kGemmEpiThreads / 32));
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();   // barriers of both CTAs initialised, tensor memory allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nnb = a.num_n_blocks, nkb = a.num_k_blocks;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = pair; ok && tile < a.num_tiles; tile += npairs) {
+        const int m0 = (tile / nnb) * 256, n0 = (tile % nnb) * BN;
+        for (int kb = 0; kb < nkb; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, a.err)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kGemm2StageBytes);
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(&tmA, fb, sA + stage * kGemm2ABytes, kb * kGemmBK, m0 + (int)rank * 128);
+          tma_load_2d_pair(&tmB, fb, sB + stage * kGemm2BBytes, kb * kGemmBK, n0 + (int)rank * 128);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader)
+      constexpr uint32_t idesc = idesc_bf16_f32(256, BN, 0, 0);
+      const uint32_t hi = kSdescHiSw128;
+      const uint32_t a_lo = sdesc_lo(smem_u32(sA), 16), b_lo = sdesc_lo(smem_u32(sB), 16);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      for (int tile = pair; ok && tile < a.num_tiles; tile += npairs) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, a.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nkb; kb++) {
+          if (!mbar_wait(&full[stage], phase, a.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ad = a_lo + (uint32_t)(stage * (kGemm2ABytes >> 4));
+          const uint32_t bd = b_lo + (uint32_t)(stage * (kGemm2BBytes >> 4));
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; k++)   // 32 bytes of K per MMA: +2
+            umma_bf16_ss_lo_pair(d_tmem, ad + 2 * k, bd + 2 * k, hi, idesc, (kb | k) != 0);
+          umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 0));
+        umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // every MMA issued has completed before the pair's tensor memory is released
+      umma_commit_pair(mapa_shared(smem_u32(done), 0));
+      mbar_wait_for(done, 0, kWaitTimeoutNs);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..9 of both CTAs
+    const int sub = warp & 3;          // TMEM lanes 32*sub .. 32*sub+31
+    const int half = (warp - 2) >> 2;  // column half of the tile
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < a.num_tiles; tile += npairs) {
+      const int m0 = (tile / nnb) * 256 + (int)rank * 128, n0 = (tile % nnb) * BN;
+      if (!mbar_wait(&tfull[acc], acc_phase, a.err)) { ok = false; break; }
+      tc_fence_after();
+      if (EPI == WX_EPI_F32_RESID) {
+        // the residual rows of this warp's next tile, into L2 while this tile drains
+        const int nt = tile + npairs;
+        if (nt < a.num_tiles) {
+          const int prow = (nt / nnb) * 256 + (int)rank * 128 + sub * 32 + lane;
+          const int pn = (nt % nnb) * BN + half * (BN / 2);
+          if (prow < a.M) {
+            const float* base = a.R + (int64_t)prow * a.ldr + pn;
+#pragma unroll
+            for (int q = 0; q < BN / 64; q++)
+              if (pn + q * 32 < a.N) prefetch_l2(base + q * 32);
+          }
+        }
+      }
+      const int row = m0 + sub * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); c++) {
+        const int n = n0 + c * 32;
+        if (n >= a.N) break;  // uniform across the warp
+        uint32_t r[32];
+        tmem_ld32(t_row + (uint32_t)(c * 32), r);
+        tmem_wait_ld();
+        if (row < a.M) epilogue_store32<EPI>(a, row, n, n + 32 <= a.N, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  // On a failed wait, loads this CTA issued may still be landing in its
+  // shared memory: give them 50 us before the pair retires.
+  if (!ok || (a.err && *reinterpret_cast<volatile int*>(a.err) != 0)) {
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 50000ull) __nanosleep(1000);
+  }
+  tc_fence_before();
+  cluster_sync_all();   // no MMA reads this CTA's shared memory or tensor memory any more
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
+  }
+}
+
+static int gemm_prepare(int bn, int epi, bool pair);
+
+// CTA pairs (the 2-SM kernel) when the 256 x 256 tiles fill every SM pair at
+// least once; smaller problems spread better over single-SM tiles.
+static bool use_pair(int64_t M, int64_t N, int nsm) {
+  return N > 128 && ((M + 255) / 256) * ((N + 255) / 256) >= nsm / 2;
+}
 
 // Build the tensor maps and launch arguments once; the encoder keeps plans for
 // its fixed buffers, the standalone entry point builds one per call.
@@ -337,20 +586,21 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
   int bn = force_bn;
   if (bn == 0) bn = (mb * ((N + 255) / 256) >= nsm && N > 128) ? 256 : 128;
   if (bn != 128 && bn != 256) return fail(WX_ERR_INVALID, "gemm: BN %d", bn);
+  const bool pair = force_bn == 0 && use_pair(M, N, nsm);
   int* err = device_error_word();
   if (!err) return fail(WX_ERR_CUDA, "gemm: device error word unavailable");
   WX_TRY(encode_tensor_map_2d(&p->tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
                               (uint64_t)M, (uint64_t)lda * 2, kGemmBK, kGemmBM,
                               CU_TENSOR_MAP_SWIZZLE_128B));
   WX_TRY(encode_tensor_map_2d(&p->tmB, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
-                              (uint64_t)N, (uint64_t)ldb * 2, kGemmBK, (uint32_t)bn,
+                              (uint64_t)N, (uint64_t)ldb * 2, kGemmBK, pair ? 128u : (uint32_t)bn,
                               CU_TENSOR_MAP_SWIZZLE_128B));
   GemmArgs& g = p->args;
   g.M = (int)M;
   g.N = (int)N;
   g.K = (int)K;
   g.num_n_blocks = (int)((N + bn - 1) / bn);
-  g.num_tiles = (int)(mb * g.num_n_blocks);
+  g.num_tiles = (int)((pair ? (M + 255) / 256 : mb) * g.num_n_blocks);
   g.num_k_blocks = (int)((K + kGemmBK - 1) / kGemmBK);
   g.C = C;
   g.ldc = ldc;
@@ -363,8 +613,9 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
   g.pos_T = 1;
   p->bn = bn;
   p->epi = epi;
-  p->grid = g.num_tiles < nsm ? g.num_tiles : nsm;
-  return gemm_prepare(bn, epi);
+  p->pair = pair;
+  p->grid = pair ? 2 * std::min(g.num_tiles, nsm / 2) : std::min(g.num_tiles, nsm);
+  return gemm_prepare(bn, epi, pair);
 }
 
 // The same plan without the library's device error word, whose first use on
@@ -389,18 +640,19 @@ int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, cons
   const int nsm = sm_count();
   const int64_t mb = (M + kGemmBM - 1) / kGemmBM;
   const int bn = (mb * ((N + 255) / 256) >= nsm && N > 128) ? 256 : 128;  // as gemm_plan
+  const bool pair = use_pair(M, N, nsm);
   WX_TRY(encode_tensor_map_2d(&p->tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
                               (uint64_t)M, (uint64_t)lda * 2, kGemmBK, kGemmBM,
                               CU_TENSOR_MAP_SWIZZLE_128B));
   WX_TRY(encode_tensor_map_2d(&p->tmB, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
-                              (uint64_t)N, (uint64_t)ldb * 2, kGemmBK, (uint32_t)bn,
+                              (uint64_t)N, (uint64_t)ldb * 2, kGemmBK, pair ? 128u : (uint32_t)bn,
                               CU_TENSOR_MAP_SWIZZLE_128B));
   GemmArgs& g = p->args;
   g.M = (int)M;
   g.N = (int)N;
   g.K = (int)K;
   g.num_n_blocks = (int)((N + bn - 1) / bn);
-  g.num_tiles = (int)(mb * g.num_n_blocks);
+  g.num_tiles = (int)((pair ? (M + 255) / 256 : mb) * g.num_n_blocks);
   g.num_k_blocks = (int)((K + kGemmBK - 1) / kGemmBK);
   g.C = C;
   g.ldc = ldc;
@@ -413,8 +665,9 @@ int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, cons
   g.pos_T = 1;
   p->bn = bn;
   p->epi = epi;
-  p->grid = g.num_tiles < nsm ? g.num_tiles : nsm;
-  return gemm_prepare(bn, epi);
+  p->pair = pair;
+  p->grid = pair ? 2 * std::min(g.num_tiles, nsm / 2) : std::min(g.num_tiles, nsm);
+  return gemm_prepare(bn, epi, pair);
 }
 
 template <int BN, int EPI>
@@ -429,8 +682,24 @@ static int set_attr_t() {
   return WX_OK;
 }
 
+template <int EPI>
+static int set_attr_pair_t() {
+  static bool done[64] = {false};
+  int dev = 0;
+  WX_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 64 && done[dev]) return WX_OK;
+  WX_CUDA_TRY(cudaFuncSetAttribute(gemm2_bf16_kernel<EPI>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kGemm2Smem));
+  if (dev < 64) done[dev] = true;
+  return WX_OK;
+}
+
 template <int BN, int EPI>
 static int launch_t(const GemmPlan& p, cudaStream_t st) {
+  if (p.pair) {
+    gemm2_bf16_kernel<EPI><<<p.grid, kGemmThreads, kGemm2Smem, st>>>(p.tmA, p.tmB, p.args);
+    return check_launch("gemm_bf16_pair");
+  }
   gemm_bf16_kernel<BN, EPI><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, st>>>(p.tmA, p.tmB,
                                                                              p.args);
   return check_launch("gemm_bf16");
@@ -438,10 +707,10 @@ static int launch_t(const GemmPlan& p, cudaStream_t st) {
 
 // Kernel attributes are set when a plan is made, so that a captured launch
 // sequence contains nothing but launches.
-static int gemm_prepare(int bn, int epi) {
+static int gemm_prepare(int bn, int epi, bool pair) {
 #define WX_GEMM_PREP(E) \
   case E:               \
-    return bn == 256 ? set_attr_t<256, E>() : set_attr_t<128, E>();
+    return pair ? set_attr_pair_t<E>() : bn == 256 ? set_attr_t<256, E>() : set_attr_t<128, E>();
   switch (epi) {
     WX_GEMM_PREP(WX_EPI_F32)
     WX_GEMM_PREP(WX_EPI_BF16)

@@ -30,6 +30,7 @@ struct GemmPlan {
   int bn;
   int grid;
   int epi;
+  bool pair;   // 2-SM kernel (CTA pairs, 256 x 256 tiles)
 };
 
 // force_bn: 0 = pick, else 128 or 256 (output columns per tile)
