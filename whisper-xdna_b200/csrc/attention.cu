@@ -3,29 +3,35 @@
 // QK -> softmax -> AV chain of the reference in one kernel, with the scores
 // and probabilities never leaving the SM.
 //
-// One CTA per (pair of 128-query tiles A and B, head, clip); 18 warps:
+// One CTA per (pair of 128-query tiles A and B, head, clip); 19 warps:
 //   warp 0     TMA: the two Q tiles once, then K and V tiles (96 keys x 64)
 //              into three-slot rings with separate K and V barriers
-//   warp 1     allocates tensor memory and issues the MMAs, per key block j:
-//              O_A += P_A(j) V_j, S_A(j+2) = Q_A K_{j+2}^T, then the same for
-//              tile B (M=128; S: N=96, K=64; PV: N=64, K=96 with P read from
-//              tensor memory and V MN-major straight from its row-major tile)
-//   warps 2-9  softmax of tile A, warps 10-17 of tile B. A query row is split
+//   warps 1-2  MMA issuers, one per query tile (warp 1 also allocates tensor
+//              memory): per key block j, O_t += P_t(j) V_j, then S_t(j+2) =
+//              Q_t K_{j+2}^T (M=128; S: N=96, K=64; PV: N=64, K=96 with P read
+//              from tensor memory and V MN-major straight from its row-major
+//              tile). One issuer per tile lets the two tiles' S -> softmax ->
+//              PV round trips overlap instead of queueing in one program order.
+//   warps 3-10 softmax of tile A, warps 11-18 of tile B. A query row is split
 //              over two warps of one tensor-memory sub-partition (keys 0-47
 //              and 48-95 of each block; O columns 0-31 and 32-63), which puts
 //              four softmax warps on every SM sub-partition; the two halves
 //              exchange their partial row maxima through shared memory at a
 //              64-thread named barrier once per block and their row sums once
-//              at the end.
+//              at the end. The tiles take turns on the SFU (A's exponentials of
+//              block j, then B's, then A's of j + 1): while one tile's warps on
+//              a sub-partition compute exponentials, the other's load S, take
+//              the row max and store P.
 //
 // Tensor memory (512 columns): S_A double-buffered at columns 0 and 96, S_B at
 // 192 and 288, O_A at 384, O_B at 448. P = exp2(s*c - m) is written back as
 // packed bf16 pairs over the S buffer it came from (keys 0-47 at columns
 // 0-23, keys 48-95 at 64-87: each half overwrites only columns it has already
 // read), and the PV MMA takes its A operand from there. The tensor core runs
-// one CTA's MMAs in issue order, so S(j+2), issued after PV(j), overwrites the
-// buffer only after PV(j) has read P(j): the softmax warps never wait for a PV
-// except to rescale O, and S(j+1) is being computed while they work on S(j).
+// one thread's MMAs in issue order, so S_t(j+2), issued by tile t's issuer
+// after PV_t(j), overwrites the buffer only after PV_t(j) has read P_t(j): the
+// softmax warps never wait for a PV except to rescale O, and S(j+1) is being
+// computed while they work on S(j).
 //
 // Online softmax with lazy rescaling: the running max m only moves when a
 // block's row max exceeds it by more than 8 (in log2 units); then O (read and
@@ -48,13 +54,13 @@ constexpr int kAttBQ = 128;                       // rows per Q tile (2 tiles pe
 constexpr int kAttBK = 96;                        // keys per block
 constexpr int kAttHD = 64;
 constexpr int kAttHalf = kAttBK / 2;              // keys per half-row warp
-constexpr int kAttThreads = 576;                  // 2 control warps + 16 softmax warps
+constexpr int kAttThreads = 608;                  // 3 control warps + 16 softmax warps
 constexpr int kAttStages = 3;                     // K and V ring slots
 constexpr int kQBytes = kAttBQ * kAttHD * 2;      // 16 KB Q tile
 constexpr int kKVBytes = kAttBK * kAttHD * 2;     // 12 KB K or V tile
 // Q_A, Q_B, the K and V rings, barriers, the row-max exchange (2 tiles x 2
 // parities x 2 halves x 128 rows of fp32)
-constexpr int kAttBarBytes = 256;
+constexpr int kAttBarBytes = 512;                // 35 mbarriers and the TMEM address
 constexpr int kAttSmem = 1024 + 2 * kQBytes + 2 * kAttStages * kKVBytes + kAttBarBytes +
                          2 * 2 * 2 * 128 * 4;
 constexpr int kAttTmemCols = 512;
@@ -64,6 +70,7 @@ constexpr int kOCol = 4 * kSBufCols;              // O_A at 384, O_B at 448
 __host__ __device__ constexpr int p_col(int half) { return half ? 64 : 0; }
 constexpr float kRescaleThreshold = 8.0f;         // log2 units
 static_assert(kOCol + 2 * kAttHD <= kAttTmemCols, "tensor memory budget");
+static_assert((1 + 4 * kAttStages + 4 + 4 + 4 + 2 + 8) * 8 + 4 <= kAttBarBytes, "barrier area");
 static_assert(2 * kQBytes % 1024 == 0 && kKVBytes % 1024 == 0, "SW128 tiles 1024-aligned");
 
 template <int N>
@@ -123,7 +130,7 @@ __device__ __forceinline__ void umma_bf16_ts_lo(uint32_t d_tmem, uint32_t a_tmem
       : "memory");
 }
 
-// 18 warps: five share a sub-partition's 16K registers, so at most 96 each.
+// 19 warps: up to five share a sub-partition's 16K registers, so at most 96 each.
 __global__ void __launch_bounds__(kAttThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmK,
@@ -147,8 +154,11 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   uint64_t* s_full = v_empty + kAttStages;             // [tile][buffer]
   uint64_t* p_full = s_full + 4;                       // [tile][block parity]
   uint64_t* o_done = p_full + 4;                       // [tile][PV parity]
-  uint64_t* done = o_done + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* done = o_done + 4;                         // [tile]
+  // SFU turns of the two tiles' warps on each sub-partition: seq[sub]
+  // completes after tile A's exponentials of a block, seq[4 + sub] after B's
+  uint64_t* seq = done + 2;                            // [direction][sub]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(seq + 8);
   float* xchg_base = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kAttBarBytes);
 
   const int warp = warp_id(), lane = lane_id();
@@ -162,16 +172,18 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     mbar_init(q_full, 1);
     for (int i = 0; i < kAttStages; i++) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
+      mbar_init(&k_empty[i], 2);   // released by both tiles' issuers
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+      mbar_init(&v_empty[i], 2);
     }
     for (int i = 0; i < 4; i++) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 256);
       mbar_init(&o_done[i], 1);
     }
-    mbar_init(done, 1);
+    mbar_init(&done[0], 1);
+    mbar_init(&done[1], 1);
+    for (int i = 0; i < 8; i++) mbar_init(&seq[i], 64);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
@@ -216,75 +228,115 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 2) {
     if (lane == 0) {
-      // ---------------- MMA issuer. The waits are blocking mbarrier
-      // try-waits, which suspend the warp instead of taking issue slots from
-      // the softmax warps that share its sub-partition.
+      // ---------------- MMA issuers: warp 1 for tile A, warp 2 for tile B, so
+      // each tile's S -> softmax -> PV round trip runs on its own and the two
+      // overlap. The tensor core runs one thread's MMAs in issue order.
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kAttBQ, kAttBK, 0, 0);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(kAttBQ, kAttHD, 0, 1);
-      // descriptor low words of the first Q tile and ring slots; every other
-      // operand is a fixed offset from these
-      const uint32_t hi = kSdescHiSw128;
-      const uint32_t q_lo = sdesc_lo(smem_u32(sQ), 16);
-      const uint32_t k_lo = sdesc_lo(smem_u32(sK), 16);
-      const uint32_t v_lo = sdesc_lo(smem_u32(sV), kKVBytes);
-      bool ok = mbar_wait(q_full, 0, a.err);
-      // S_t(j) = Q_t K_j^T into buffer j & 1; the K slot frees once tile B's
-      // product is done
-      auto issue_s = [&](int t, int j) -> bool {
-        const int s = j % kAttStages;
-        if (t == 0 && !mbar_wait(&k_full[s], (uint32_t)(j / kAttStages) & 1u, a.err)) return false;
-        tc_fence_after();
-        const uint32_t qd = q_lo + (uint32_t)(t * (kQBytes >> 4));
-        const uint32_t kd = k_lo + (uint32_t)(s * (kKVBytes >> 4));
-        const uint32_t d = tmem + (uint32_t)((2 * t + (j & 1)) * kSBufCols);
-#pragma unroll
-        for (int kk = 0; kk < kAttHD / 16; kk++)
-          umma_bf16_ss_lo(d, qd + 2 * kk, kd + 2 * kk, hi, idesc_qk, kk != 0);
-        umma_commit(&s_full[2 * t + (j & 1)]);
-        if (t == 1) umma_commit(&k_empty[s]);
-        return true;
+      // The ring slot and S buffer are fixed at compile time (the block loop is
+      // unrolled by six = three slots x two buffers), so each operand is one
+      // constant offset from these bases and each group of MMAs is one asm
+      // statement with a single pair of predicates.
+      const uint64_t q_desc = sdesc_kmajor_sw128(smem_u32(sQ));
+      const uint64_t k_desc = sdesc_kmajor_sw128(smem_u32(sK));
+      const uint64_t v_desc = sdesc_mnmajor_sw128(smem_u32(sV), kKVBytes);
+      // S_t(j) = Q_t K_j^T into buffer B from ring slot SL (K = 64: four MMAs,
+      // 32 bytes of K apart)
+      auto mma_s = [&](auto t_c, auto b_c, auto sl_c) {
+        constexpr int t = decltype(t_c)::value, b = decltype(b_c)::value,
+                      sl = decltype(sl_c)::value;
+        const uint32_t d = tmem + (uint32_t)((2 * t + b) * kSBufCols);
+        const uint64_t qa = q_desc + (uint64_t)(t * (kQBytes >> 4));
+        const uint64_t kb = k_desc + (uint64_t)(sl * (kKVBytes >> 4));
+        asm volatile(
+            "{\n\t.reg .pred pf, pt;\n\t"
+            "setp.ne.b32 pf, %1, %1;\n\t"
+            "setp.eq.b32 pt, %1, %1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %3, %1, pf;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %5, %1, pt;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %7, %1, pt;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %9, %1, pt;\n\t}\n" ::"r"(d),
+            "r"(idesc_qk), "l"(qa), "l"(kb), "l"(qa + 2), "l"(kb + 2), "l"(qa + 4), "l"(kb + 4),
+            "l"(qa + 6), "l"(kb + 6)
+            : "memory");
       };
-      // O_t += P_t(j) V_j, P from the S buffer; the V slot frees once tile B's
-      // product is done
-      auto issue_pv = [&](int t, int j) -> bool {
-        const int s = j % kAttStages;
-        if (!mbar_wait(&p_full[2 * t + (j & 1)], (uint32_t)(j >> 1) & 1u, a.err)) return false;
-        if (t == 0 && !mbar_wait(&v_full[s], (uint32_t)(j / kAttStages) & 1u, a.err)) return false;
-        tc_fence_after();
-        const uint32_t p_tmem = tmem + (uint32_t)((2 * t + (j & 1)) * kSBufCols);
-        const uint32_t vd = v_lo + (uint32_t)(s * (kKVBytes >> 4));
+      // O_t += P_t V from buffer B and ring slot SL: six MMAs of 16 keys, P
+      // read from tensor memory (keys 0-47 at columns 0-23, 48-95 at 64-87),
+      // V MN-major 2048 bytes (16 rows) apart; acc = 0 only for the first block
+      auto mma_pv = [&](auto t_c, auto b_c, auto sl_c, uint32_t acc) {
+        constexpr int t = decltype(t_c)::value, b = decltype(b_c)::value,
+                      sl = decltype(sl_c)::value;
         const uint32_t d = tmem + (uint32_t)(kOCol + t * kAttHD);
-#pragma unroll
-        for (int kk = 0; kk < kAttBK / 16; kk++) {
-          const int half = kk / (kAttHalf / 16), kh = kk % (kAttHalf / 16);
-          // 16 keys of V = 16 rows of 128 bytes = 2048 bytes further on
-          umma_bf16_ts_lo(d, p_tmem + (uint32_t)(p_col(half) + kh * 8), vd + 128 * kk, hi,
-                          idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&o_done[2 * t + (j & 1)]);
-        if (t == 1) umma_commit(&v_empty[s]);
-        return true;
+        const uint32_t pa = tmem + (uint32_t)((2 * t + b) * kSBufCols);
+        const uint64_t vb = v_desc + (uint64_t)(sl * (kKVBytes >> 4));
+        asm volatile(
+            "{\n\t.reg .pred p0, pt;\n\t"
+            "setp.ne.b32 p0, %2, 0;\n\t"
+            "setp.eq.b32 pt, %1, %1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %9, %1, p0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %10, %1, pt;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %11, %1, pt;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %12, %1, pt;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %13, %1, pt;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %14, %1, pt;\n\t}\n" ::"r"(d),
+            "r"(idesc_pv), "r"(acc), "r"(pa + p_col(0)), "r"(pa + p_col(0) + 8),
+            "r"(pa + p_col(0) + 16), "r"(pa + p_col(1)), "r"(pa + p_col(1) + 8),
+            "r"(pa + p_col(1) + 16), "l"(vb), "l"(vb + 128), "l"(vb + 256), "l"(vb + 384),
+            "l"(vb + 512), "l"(vb + 640)
+            : "memory");
       };
-      if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
-      if (ok && nkv > 1) ok = issue_s(0, 1) && issue_s(1, 1);
-      for (int j = 0; ok && j < nkv; j++) {
-        const bool more = j + 2 < nkv;
-        if (!issue_pv(0, j)) { ok = false; break; }
-        if (more && !issue_s(0, j + 2)) { ok = false; break; }
-        if (!issue_pv(1, j)) { ok = false; break; }
-        if (more && !issue_s(1, j + 2)) { ok = false; break; }
-      }
-      umma_commit(done);
-      mbar_wait_for(done, 0, kWaitTimeoutNs);
+      auto run = [&](auto t_c) {
+        constexpr int t = decltype(t_c)::value;
+        bool ok = mbar_wait(q_full, 0, a.err);
+        // S of block j (j % 6 == M) into buffer M % 2 from slot M % 3; the K
+        // slot frees once both tiles' products are done (count 2)
+        auto issue_s = [&](int j, auto mc) -> bool {
+          constexpr int m = decltype(mc)::value;
+          if (!mbar_wait(&k_full[m % 3], (uint32_t)(j / kAttStages) & 1u, a.err)) return false;
+          tc_fence_after();
+          mma_s(t_c, std::integral_constant<int, m % 2>(), std::integral_constant<int, m % 3>());
+          umma_commit(&s_full[2 * t + m % 2]);
+          umma_commit(&k_empty[m % 3]);
+          return true;
+        };
+        // Block j: PV_t(j), then S_t(j + 2) into the buffer PV_t(j) has read P from
+        auto step = [&](int j, auto mc) -> bool {
+          constexpr int m = decltype(mc)::value;
+          if (!mbar_wait(&p_full[2 * t + m % 2], (uint32_t)(j >> 1) & 1u, a.err)) return false;
+          if (!mbar_wait(&v_full[m % 3], (uint32_t)(j / kAttStages) & 1u, a.err)) return false;
+          tc_fence_after();
+          mma_pv(t_c, std::integral_constant<int, m % 2>(), std::integral_constant<int, m % 3>(),
+                 j > 0 ? 1u : 0u);
+          umma_commit(&o_done[2 * t + m % 2]);
+          umma_commit(&v_empty[m % 3]);
+          if (j + 2 < nkv) return issue_s(j + 2, std::integral_constant<int, (m + 2) % 6>());
+          return true;
+        };
+        if (ok) ok = issue_s(0, std::integral_constant<int, 0>());
+        if (ok && nkv > 1) ok = issue_s(1, std::integral_constant<int, 1>());
+        for (int j = 0; ok && j < nkv; j += 6) {
+          ok = step(j, std::integral_constant<int, 0>());
+          if (ok && j + 1 < nkv) ok = step(j + 1, std::integral_constant<int, 1>());
+          if (ok && j + 2 < nkv) ok = step(j + 2, std::integral_constant<int, 2>());
+          if (ok && j + 3 < nkv) ok = step(j + 3, std::integral_constant<int, 3>());
+          if (ok && j + 4 < nkv) ok = step(j + 4, std::integral_constant<int, 4>());
+          if (ok && j + 5 < nkv) ok = step(j + 5, std::integral_constant<int, 5>());
+        }
+        // every MMA of this issuer has completed before tensor memory is released
+        umma_commit(&done[t]);
+        mbar_wait_for(&done[t], 0, kWaitTimeoutNs);
+      };
+      if (warp == 1) run(std::integral_constant<int, 0>());
+      else run(std::integral_constant<int, 1>());
     }
   } else {
     // ---------------- softmax: warps 2-9 tile A, 10-17 tile B. Each query row
     // is split over two warps of the same TMEM sub-partition: half 0 takes keys
     // 0-47 of every block and O columns 0-31, half 1 keys 48-95 and O 32-63.
-    const int t = (warp - 2) >> 3;
-    const int half = ((warp - 2) & 7) >> 2;
+    const int t = (warp - 3) >> 3;
+    const int half = ((warp - 3) & 7) >> 2;
     const int sub = warp & 3;
     const int r = sub * 32 + lane;  // row within the tile
     const uint32_t t_lane = tmem + ((uint32_t)(sub * 32) << 16);
@@ -311,14 +363,14 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       tmem_wait_ld();
       float mx;
       if (kvalid >= kAttHalf) {
-        float mm[8];
+        float mm[8];   // three-input max: 24 instructions for 48 values
 #pragma unroll
         for (int i = 0; i < 8; i++)
-          mm[i] = fmaxf(fmaxf(__uint_as_float(s[i]), __uint_as_float(s[i + 8])),
-                        fmaxf(fmaxf(__uint_as_float(s[i + 16]), __uint_as_float(s[i + 24])),
-                              fmaxf(__uint_as_float(s[i + 32]), __uint_as_float(s[i + 40]))));
-        mx = fmaxf(fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3])),
-                   fmaxf(fmaxf(mm[4], mm[5]), fmaxf(mm[6], mm[7])));
+          mm[i] = fmax3(fmax3(__uint_as_float(s[i]), __uint_as_float(s[i + 8]),
+                              __uint_as_float(s[i + 16])),
+                        __uint_as_float(s[i + 24]),
+                        fmaxf(__uint_as_float(s[i + 32]), __uint_as_float(s[i + 40])));
+        mx = fmax3(fmax3(mm[0], mm[1], mm[2]), fmax3(mm[3], mm[4], mm[5]), fmaxf(mm[6], mm[7]));
       } else {
         mx = -INFINITY;
 #pragma unroll
@@ -350,8 +402,17 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           sums[(i / 2) & 3] += p0 + p1;
         }
       };
+      // SFU turns (seq): tile A's exponentials of block j wait for tile B's of
+      // block j - 1 and tile B's for tile A's of block j. Every wait is
+      // unambiguous: a tile cannot finish two turns before the other has one.
+      if (t == 0) {
+        if (j > 0 && !mbar_wait(&seq[4 + sub], (uint32_t)(j - 1) & 1u, a.err)) ok = false;
+      } else {
+        if (!mbar_wait(&seq[sub], (uint32_t)j & 1u, a.err)) ok = false;
+      }
       if (kvalid >= kAttHalf) make_p(std::false_type());
       else make_p(std::true_type());
+      mbar_arrive(&seq[t * 4 + sub]);
       const uint32_t t_p = t_buf + (uint32_t)p_col(half);
       tmem_st16(t_p, pw);
       tmem_st8(t_p + 16, pw + 16);
@@ -373,6 +434,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       mbar_arrive(&p_full[2 * t + (j & 1)]);
       l = l * corr + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
     }
+    // tile B's last turn is consumed, so no phase is left pending at exit
+    if (t == 0 && !mbar_wait(&seq[4 + sub], (uint32_t)(nkv - 1) & 1u, a.err)) ok = false;
     if (ok) ok = mbar_wait(&o_done[2 * t + ((nkv - 1) & 1)], (uint32_t)((nkv - 1) >> 1) & 1u, a.err);
     // the row sum is the sum of the two halves' sums
     float* lslot = xchg + (nkv & 1) * 256;
