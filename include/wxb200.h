@@ -213,6 +213,15 @@ int wx_encoder_forward_host(wx_encoder* enc, const float* mel_host, float* out_h
 /* Device memory the encoder holds (weights + workspace), in bytes. */
 int64_t wx_encoder_device_bytes(const wx_encoder* enc);
 
+/* Diagnostic: exercises the bounded-wait failure path of the kernels. One
+ * thread waits, through the same helper every kernel wait uses, on an mbarrier
+ * that nothing completes; after limit_ns (0 < limit_ns <= 2e9) it records
+ * WX_DEVERR_TIMEOUT in the device error word and the kernel returns, leaving
+ * the context usable. Read and clear the word with wx_device_error. Replaces
+ * no reference interface (the reference's failure path is host-side:
+ * serve/npu_stt_server.py:128-129 injects failures on the host). */
+int wx_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

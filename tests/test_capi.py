@@ -64,6 +64,15 @@ def test_gelu_table_matches_oracle(wxlib, mode):
     assert np.array_equal(t, exp)
 
 
+def test_selftest_limits_checked_without_a_gpu(wxlib):
+    """The wait-timeout diagnostic validates its limit before touching a device."""
+    import ctypes
+    fn = wxlib.wx_selftest_wait_timeout
+    fn.restype, fn.argtypes = ctypes.c_int, [ctypes.c_uint64, ctypes.c_void_p]
+    assert fn(0, None) == -1
+    assert fn(3_000_000_000, None) == -1
+
+
 def test_invalid_arguments_rejected_before_any_launch(wxlib):
     from wxb200 import _lib as L
     nul = ctypes.c_void_p(0)

@@ -5,6 +5,7 @@
 #include <mutex>
 #include <vector>
 
+#include "common.cuh"
 #include "wxb200_internal.h"
 
 namespace wx {
@@ -117,3 +118,34 @@ int wx_device_error(int* flags, int clear) {
 }
 
 }  // extern "C"
+
+// A kernel whose one waiting thread waits, through the same bounded-wait
+// helper the kernels use, on an mbarrier that nothing ever completes: after
+// limit_ns it records WX_DEVERR_TIMEOUT in the device error word and returns.
+// It exercises the failure path of every kernel wait without a GPU fault; the
+// context stays usable.
+namespace wx {
+__global__ void selftest_wait_timeout_kernel(int* err, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = mbar_wait_limit(&bar, 0, err, limit_ns);   // never completes
+    if (ok) set_device_error(err, 0x40000000);                 // would be a logic error
+  }
+  __syncthreads();
+}
+}  // namespace wx
+
+extern "C" int wx_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 2000000000ull)
+    return wx::fail(WX_ERR_INVALID, "selftest: limit_ns must be in (0, 2e9]");
+  int* w = wx::device_error_word();
+  if (!w) return wx::fail(WX_ERR_CUDA, "device error word unavailable");
+  wx::selftest_wait_timeout_kernel<<<1, 32, 0, wx::as_stream(stream)>>>(w, limit_ns);
+  return wx::check_launch("selftest_wait_timeout");
+}
+

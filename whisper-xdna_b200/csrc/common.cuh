@@ -258,7 +258,8 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, ui
 // Wait for the phase with the given parity to complete. Bounded: returns false
 // (and records a timeout) if it has not after kWaitTimeoutNs, or at once if
 // another thread of this kernel has already recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* err,
+                                                uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -266,11 +267,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     for (int i = 0; i < 32; i++)
       if (mbar_try_wait(bar, parity)) return true;
     if (err && *reinterpret_cast<volatile int*>(err) != 0) return false;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       set_device_error(err, WX_DEVERR_TIMEOUT);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait_limit(bar, parity, err, kWaitTimeoutNs);
 }
 
 // ---------------------------------------------------------------- TMA
