@@ -349,7 +349,7 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 // TMA tile load into this CTA's shared memory, completing on an mbarrier that
-// may be the peer CTA's (cta_group::2 form; not a multicast)
+// may be the peer CTA's (the cta_group::2 form: one destination, this CTA)
 __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster,
                                                  void* dst, int x, int y) {
   asm volatile(
