@@ -83,6 +83,31 @@ def test_device_forward_matches_host_forward(cuda):
     assert np.array_equal(dev.cpu().numpy(), host)
 
 
+@pytest.mark.parametrize("batch", [31, 32, 33])
+def test_pipelined_host_forward_matches_device_forward(cuda, batch):
+    """forward_host runs batches of 32 or more in two halves with the copies
+    overlapping compute (31 -> one chunk, 32 -> 16+16, 33 -> 17+16); every clip
+    equals the one-launch device forward of the whole batch."""
+    W = R.make_weights("tiny", seed=5, n_layer=2)
+    mels = np.stack([R.make_mel(80, 400, seed=40 + i) for i in range(batch)])
+    enc = Encoder(W, n_layer=2, max_batch=batch)
+    try:
+        pinned = torch.from_numpy(mels).pin_memory()
+        out = torch.empty(batch, 200, 384).pin_memory()
+        host = enc.forward_host(pinned.numpy(), out=out.numpy())
+        dev = enc.forward(torch.from_numpy(mels).cuda())
+        torch.cuda.synchronize()
+        ref = dev.cpu().numpy()
+        for i in range(batch):
+            assert np.allclose(host[i], ref[i], rtol=1e-5, atol=1e-5), i
+            assert R.cosine(host[i], ref[i]) >= 0.999999
+        again = enc.forward_host(pinned.numpy(), out=out.numpy())   # graphs replayed
+        assert np.array_equal(again, host)
+    finally:
+        enc.close()
+    assert L.device_error() == 0
+
+
 def test_dropin_encoder_signature(cuda):
     """encoder(W, mel, RT.matmul, RT.matmul, ..., attn_fn=RT.attn_chain,
     mlp_fn=RT.mlp, fold_bias=True) -- the server's call (serve/npu_stt_server.py:340-342)."""

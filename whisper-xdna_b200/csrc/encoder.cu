@@ -148,6 +148,12 @@ struct wx_encoder {
   std::map<wx::GraphKey, cudaGraphExec_t> graphs;
   cudaStream_t side = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  // the host-buffer entry point's pipeline: copy-in, compute and copy-out
+  // streams, and per-chunk events
+  static constexpr int kHostChunks = 2;
+  cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+  cudaEvent_t ev_h2d[kHostChunks] = {}, ev_done[kHostChunks] = {};
   std::mutex mu;
 };
 
@@ -332,10 +338,18 @@ int wx_encoder_create(wx_encoder** out, int n_mels, int d_model, int n_head, int
   e->stage_n = std::max((int64_t)ffn * d, std::max(3 * d * d, T * d));
   A((void**)&e->stage, e->stage_n * 4);
   if (s == WX_OK) {
-    if (cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&e->ev_in, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&e->ev_out, cudaEventDisableTiming) != cudaSuccess)
-      s = fail(WX_ERR_CUDA, "encoder_create: stream/event creation failed");
+    bool good = cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking) == cudaSuccess &&
+                cudaEventCreateWithFlags(&e->ev_in, cudaEventDisableTiming) == cudaSuccess &&
+                cudaEventCreateWithFlags(&e->ev_out, cudaEventDisableTiming) == cudaSuccess &&
+                cudaStreamCreateWithFlags(&e->s_in, cudaStreamNonBlocking) == cudaSuccess &&
+                cudaStreamCreateWithFlags(&e->s_comp, cudaStreamNonBlocking) == cudaSuccess &&
+                cudaStreamCreateWithFlags(&e->s_out, cudaStreamNonBlocking) == cudaSuccess &&
+                cudaEventCreateWithFlags(&e->ev_start, cudaEventDisableTiming) == cudaSuccess &&
+                cudaEventCreateWithFlags(&e->ev_end, cudaEventDisableTiming) == cudaSuccess;
+    for (int k = 0; good && k < wx_encoder::kHostChunks; k++)
+      good = cudaEventCreateWithFlags(&e->ev_h2d[k], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&e->ev_done[k], cudaEventDisableTiming) == cudaSuccess;
+    if (!good) s = fail(WX_ERR_CUDA, "encoder_create: stream/event creation failed");
   }
   if (s != WX_OK) {
     wx_encoder_destroy(e);
@@ -353,6 +367,14 @@ int wx_encoder_destroy(wx_encoder* e) {
   if (e->side) cudaStreamDestroy(e->side);
   if (e->ev_in) cudaEventDestroy(e->ev_in);
   if (e->ev_out) cudaEventDestroy(e->ev_out);
+  for (cudaStream_t x : {e->s_in, e->s_comp, e->s_out})
+    if (x) cudaStreamDestroy(x);
+  for (cudaEvent_t x : {e->ev_start, e->ev_end})
+    if (x) cudaEventDestroy(x);
+  for (int k = 0; k < wx_encoder::kHostChunks; k++) {
+    if (e->ev_h2d[k]) cudaEventDestroy(e->ev_h2d[k]);
+    if (e->ev_done[k]) cudaEventDestroy(e->ev_done[k]);
+  }
   delete e;
   return WX_OK;
 }
@@ -469,11 +491,35 @@ int wx_encoder_forward_host(wx_encoder* e, const float* mel_host, float* out_hos
     return fail(WX_ERR_INVALID, "encoder_forward_host: bad batch or n_frames");
   cudaStream_t st = as_stream(stream);
   const int64_t T = n_frames / 2;
-  const size_t in_bytes = (size_t)batch * e->n_mels * n_frames * 4;
-  const size_t out_bytes = (size_t)batch * T * e->d * 4;
-  WX_CUDA_TRY(cudaMemcpyAsync(e->mel_dev, mel_host, in_bytes, cudaMemcpyHostToDevice, st));
-  WX_TRY(wx_encoder_forward(e, e->mel_dev, e->out_dev, batch, n_frames, use_graph, stream));
-  WX_CUDA_TRY(cudaMemcpyAsync(out_host, e->out_dev, out_bytes, cudaMemcpyDeviceToHost, st));
+  const size_t in_clip = (size_t)e->n_mels * n_frames, out_clip = (size_t)T * e->d;
+  // Batches of 32 clips or more run in two halves: the second half's mel goes
+  // in on s_in while the first computes on s_comp, and the first half's
+  // features come out on s_out while the second computes, so about half of
+  // the copies hide behind compute. (Smaller chunks hide more of the copies
+  // but cost more than they hide: at 16 clips the out-proj and fc2 GEMMs lose
+  // ~9% to the last partial wave of tiles.) Chunks use disjoint parts of the
+  // staging buffers and run one after the other through the shared workspace.
+  const int64_t chunk = batch >= 32 ? (batch + 1) / 2 : batch;
+  WX_CUDA_TRY(cudaEventRecord(e->ev_start, st));
+  for (cudaStream_t x : {e->s_in, e->s_comp, e->s_out})
+    WX_CUDA_TRY(cudaStreamWaitEvent(x, e->ev_start, 0));
+  int k = 0;
+  for (int64_t b0 = 0; b0 < batch; b0 += chunk, k++) {
+    const int64_t nb = std::min(chunk, batch - b0);
+    float* md = e->mel_dev + b0 * in_clip;
+    float* od = e->out_dev + b0 * out_clip;
+    WX_CUDA_TRY(cudaMemcpyAsync(md, mel_host + b0 * in_clip, nb * in_clip * 4,
+                                cudaMemcpyHostToDevice, e->s_in));
+    WX_CUDA_TRY(cudaEventRecord(e->ev_h2d[k], e->s_in));
+    WX_CUDA_TRY(cudaStreamWaitEvent(e->s_comp, e->ev_h2d[k], 0));
+    WX_TRY(wx_encoder_forward(e, md, od, nb, n_frames, use_graph, e->s_comp));
+    WX_CUDA_TRY(cudaEventRecord(e->ev_done[k], e->s_comp));
+    WX_CUDA_TRY(cudaStreamWaitEvent(e->s_out, e->ev_done[k], 0));
+    WX_CUDA_TRY(cudaMemcpyAsync(out_host + b0 * out_clip, od, nb * out_clip * 4,
+                                cudaMemcpyDeviceToHost, e->s_out));
+  }
+  WX_CUDA_TRY(cudaEventRecord(e->ev_end, e->s_out));
+  WX_CUDA_TRY(cudaStreamWaitEvent(st, e->ev_end, 0));
   WX_CUDA_TRY(cudaStreamSynchronize(st));
   return WX_OK;
 }
