@@ -213,6 +213,17 @@ int wx_encoder_forward_host(wx_encoder* enc, const float* mel_host, float* out_h
 /* Device memory the encoder holds (weights + workspace), in bytes. */
 int64_t wx_encoder_device_bytes(const wx_encoder* enc);
 
+/* whisper's log-mel frontend: audio (batch clips, row stride ld_audio floats,
+ * the first n_samples of each at 16 kHz, zero-padded or trimmed to 30 s) ->
+ * mel_out (batch, n_mels, 3000) fp32, all device memory. Centred STFT (n_fft
+ * 400, hop 160, periodic Hann, reflect padding), power spectrum, Slaney mel
+ * filterbank (n_mels 80 or 128, 0-8 kHz), log10(max(., 1e-10)), floor at the
+ * clip's maximum - 8, (x + 4) / 4. Replaces openai-whisper's
+ * log_mel_spectrogram(pad_or_trim(audio), n_mels) as the reference server calls
+ * it (serve/npu_stt_server.py:334-336). mel_out must be 16-byte aligned. */
+int wx_log_mel(const float* audio, int64_t batch, int64_t n_samples, int64_t ld_audio,
+               int n_mels, float* mel_out, void* stream);
+
 /* Diagnostic: exercises the bounded-wait failure path of the kernels. One
  * thread waits, through the same helper every kernel wait uses, on an mbarrier
  * that nothing completes; after limit_ns (0 < limit_ns <= 2e9) it records

@@ -18,7 +18,8 @@ CSRC = PKG.parent / "csrc"
 ROOT = PKG.parents[1]
 BUILD = ROOT / "_build"
 LIB = PKG / "libwxb200.so"
-SOURCES = ["capi.cu", "rowops.cu", "gemm.cu", "attention.cu", "encoder.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "rowops.cu", "gemm.cu", "attention.cu", "encoder.cu", "noalloc.cu",
+           "mel.cu"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3",
               "-std=c++17", "-Xcompiler", "-fPIC"]
 

@@ -54,6 +54,7 @@ SIGNATURES = {
     "wx_encoder_forward": (_i, [_p, _p, _p, _i64, _i64, _i, _p]),
     "wx_encoder_forward_host": (_i, [_p, _p, _p, _i64, _i64, _i, _p]),
     "wx_encoder_device_bytes": (_i64, [_p]),
+    "wx_log_mel": (_i, [_p, _i64, _i64, _i64, _i, _p, _p]),
     "wx_selftest_wait_timeout": (_i, [_c.c_uint64, _p]),
 }
 

@@ -5,7 +5,9 @@
 Kernels: attention, fc1 (GEMM + GELU), fc2 (GEMM + residual), qkv, outproj,
 layernorm (fp32 -> bf16, the encoder's), and the standalone row ops at the
 BASELINE row-op sizes: gelu (g4r 1500x5120), gelu_f32 (g4f 1500x5120), softmax
-(s4r 20x1500x1500, scale 1/8), layernorm_gb (1500x1280 with gamma/beta).
+(s4r 20x1500x1500, scale 1/8), layernorm_gb (1500x1280 with gamma/beta), and
+log_mel (batch clips of 30 s audio -> 128 x 3000 features; FLOP = the direct
+DFT's 4 per sample, bin and frame).
 Each launch is timed with CUDA events on the launching stream after warm-up;
 with --flush the L2 (126 MB) is overwritten between launches, which the row
 ops need since their inputs fit in L2. Prints one JSON line.
@@ -74,6 +76,12 @@ def setup(kernel, batch, dev="cuda"):
         fn = lambda: ops.layer_norm_rows(x, gm, bt, out=y, mode=L.WX_LN_AIE,
                                          rounding=L.WX_ROUND_RNE)
         return fn, 0.0, x.numel() * 4 + 2 * 1280 * 4
+    if kernel == "log_mel":
+        # batch clips of 30 s audio -> (batch, 128, 3000) features
+        a = rn(batch, 480000, sc=0.1)
+        y = torch.empty(batch, 128, 3000, device=dev)
+        fn = lambda: ops.log_mel(a, n_mels=128, out=y)
+        return fn, batch * 3000 * 201 * 400 * 4.0, batch * (480000 + 128 * 3000) * 4
     raise ValueError(f"unknown kernel {kernel!r}")
 
 

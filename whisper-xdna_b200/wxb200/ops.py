@@ -134,3 +134,21 @@ def attention(q, k, v, n_batch, n_head, scale, out=None):
                                  q.stride(0), k.stride(0), v.stride(0), out.stride(0),
                                  float(scale), _stream()))
     return out
+
+
+def log_mel(audio, n_mels=80, out=None):
+    """whisper's log-mel features of 16 kHz audio on the GPU: audio a CUDA
+    float32 tensor (batch, n_samples) or (n_samples,), each clip zero-padded or
+    trimmed to 30 s -> (batch, n_mels, 3000) float32 (or (n_mels, 3000))."""
+    squeeze = audio.dim() == 1
+    a = audio.unsqueeze(0) if squeeze else audio
+    if not a.is_cuda or a.dtype != torch.float32 or a.dim() != 2 or a.stride(1) != 1:
+        raise ValueError("audio must be a CUDA float32 tensor with contiguous rows")
+    B, n = a.shape
+    if out is None:
+        out = torch.empty(B, n_mels, 3000, dtype=torch.float32, device=a.device)
+    if out.shape != (B, n_mels, 3000) or not out.is_contiguous() or out.dtype != torch.float32:
+        raise ValueError("out must be a contiguous float32 (batch, n_mels, 3000) tensor")
+    L.check(L.lib().wx_log_mel(_ptr(a), B, n, a.stride(0) if B > 1 else n, int(n_mels),
+                               _ptr(out), _stream()))
+    return out[0] if squeeze else out
