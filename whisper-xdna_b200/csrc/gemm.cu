@@ -23,6 +23,7 @@
 // (ones column on A, bias row on B, src/rawxrt.py:352-371) becomes a bias
 // added to the fp32 accumulator in the epilogue.
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 #include "plans.cuh"
@@ -154,6 +155,94 @@ __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int row, int
 #pragma unroll
       for (int j = 0; j < 32; j++)
         if (n + j < a.N) c[j] = (uint16_t)bf16_bits<RND_RNE>(v[j]);
+    }
+  }
+}
+
+// Epilogues that the 2-SM kernel writes through shared memory and TMA stores:
+// each epilogue warp stages 32 rows x 128 bytes of its share of the tile (32
+// fp32 or 64 bf16 columns) and stores the box with one bulk tensor copy; the
+// residual of WX_EPI_F32_RESID arrives in the same buffer by a TMA load two
+// chunks ahead. Row-per-thread global accesses (one 16-byte piece of 32
+// different rows per instruction) cost a wavefront per sector, which the
+// short-K residual GEMMs could not hide behind their MMAs.
+template <int EPI>
+struct TmaEpi {
+  static constexpr bool kOn = EPI == WX_EPI_F32 || EPI == WX_EPI_F32_RESID || EPI == WX_EPI_BF16 ||
+                              EPI == WX_EPI_BF16_GELU || EPI == WX_EPI_BF16_GELU_ERF;
+  static constexpr bool kF32 = EPI == WX_EPI_F32 || EPI == WX_EPI_F32_RESID;
+  static constexpr int kCols = kF32 ? 32 : 64;   // columns of one 128-byte staged row
+};
+constexpr int kEpiBufBytes = 32 * 128;   // one warp's chunk: 32 rows x 128 bytes
+
+__device__ __forceinline__ void add_bias32(const GemmArgs& a, int n, float (&v)[32]) {
+  if (!a.bias) return;
+  if (n + 32 <= a.N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(a.bias + n + j));
+      v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      if (n + j < a.N) v[j] += a.bias[n + j];
+  }
+}
+
+// One chunk of a warp's share of the tile into its staging buffer, thread =
+// row: `rowp` is this thread's 128-byte row, whose 16-byte unit j sits at unit
+// j ^ (row & 7) (the 128-byte swizzle of the tensor maps, so that the eight
+// threads of each shared-memory phase hit eight different bank groups).
+// t_col: tensor-memory address of the chunk's first column for this warp's
+// lanes; n: its first output column. WX_EPI_F32_RESID finds the residual in
+// the buffer and adds it.
+template <int EPI>
+__device__ __forceinline__ void epi_chunk_to_smem(const GemmArgs& a, uint32_t t_col, int n,
+                                                  uint8_t* rowp, int lane) {
+  const int sw = lane & 7;
+  if constexpr (TmaEpi<EPI>::kF32) {
+    uint32_t r[32];
+    tmem_ld32(t_col, r);
+    tmem_wait_ld();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+    add_bias32(a, n, v);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      float4* p = reinterpret_cast<float4*>(rowp + ((j ^ sw) << 4));
+      if constexpr (EPI == WX_EPI_F32_RESID) {
+        const float4 t = *p;
+        v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+      }
+      *p = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+  } else {
+    uint32_t r0[32], r1[32];
+    tmem_ld32(t_col, r0);
+    tmem_ld32(t_col + 32, r1);
+    tmem_wait_ld();
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] = __uint_as_float(h ? r1[j] : r0[j]);
+      add_bias32(a, n + 32 * h, v);
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        if constexpr (EPI == WX_EPI_BF16_GELU)   // g4f: rne(x), then poly4 on packed pairs
+          w[j] = gelu_poly4_bf16x2_rne(pack_bf16x2_rne(v[2 * j], v[2 * j + 1]));
+        else if constexpr (EPI == WX_EPI_BF16_GELU_ERF)
+          w[j] = pack_bf16x2_rne(gelu_erf(v[2 * j]), gelu_erf(v[2 * j + 1]));
+        else
+          w[j] = pack_bf16x2_rne(v[2 * j], v[2 * j + 1]);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+        *reinterpret_cast<uint4*>(rowp + (((4 * h + q) ^ sw) << 4)) =
+            make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
     }
   }
 }
@@ -325,13 +414,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //              and to the peer's barrier (two commits, same offset)
 //   tfull[b]   both CTAs, committed like empty
 //   tempty[b]  leader only: one arrival per epilogue warp of either CTA
+//   rfull[w][b] WX_EPI_F32_RESID: residual chunk landed in buffer b of
+//              epilogue warp w
 // Every wait is bounded; both CTAs always reach the final cluster barrier,
-// after which the tensor memory of the pair is released.
-constexpr int kGemm2Stages = 6;
+// after which the tensor memory of the pair is released. With the TMA
+// epilogue the ring has five stages (160 KB) beside the 64 KB of staging
+// buffers (8 warps x 2 x 4 KB); otherwise six.
 constexpr int kGemm2ABytes = 128 * kGemmBK * 2;                   // 16 KB
 constexpr int kGemm2BBytes = 128 * kGemmBK * 2;                   // 16 KB (half of N=256)
 constexpr int kGemm2StageBytes = kGemm2ABytes + kGemm2BBytes;
-constexpr int kGemm2Smem = kGemm2Stages * kGemm2StageBytes + 1024 + 256;
+constexpr int kGemm2EpiBytes = (kGemmEpiThreads / 32) * 2 * kEpiBufBytes;
+constexpr int kGemm2BarBytes = 512;
+template <int EPI>
+struct Gemm2Cfg {
+  static constexpr int STAGES = TmaEpi<EPI>::kOn ? 5 : 6;
+  static constexpr int EPI_BYTES = TmaEpi<EPI>::kOn ? kGemm2EpiBytes : 0;
+  static constexpr int SMEM = STAGES * kGemm2StageBytes + EPI_BYTES + 1024 + kGemm2BarBytes;
+  static_assert(SMEM <= 232448, "2-SM GEMM shared memory");
+};
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -401,21 +501,27 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
-                      const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
-  constexpr int S = kGemm2Stages;
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmC,
+                      const __grid_constant__ CUtensorMap tmR, const GemmArgs a) {
+  using Cfg = Gemm2Cfg<EPI>;
+  constexpr int S = Cfg::STAGES;
   constexpr int BN = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * kGemm2ABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kGemm2StageBytes);
+  uint8_t* sE = smem + S * kGemm2StageBytes;   // epilogue staging (TMA epilogues)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sE + Cfg::EPI_BYTES);
   uint64_t* full = bars;            // [S], used in the leader
   uint64_t* empty = bars + S;       // [S]
   uint64_t* tfull = bars + 2 * S;   // [2]
   uint64_t* tempty = tfull + 2;     // [2], used in the leader
   uint64_t* done = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* rfull = done + 1;       // [8 warps][2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + 2 * (kGemmEpiThreads / 32));
+  static_assert((2 * S + 5 + 2 * (kGemmEpiThreads / 32)) * 8 + 4 <= kGemm2BarBytes, "barriers");
 
   const int warp = warp_id(), lane = lane_id();
   const uint32_t rank = cluster_rank();
@@ -430,9 +536,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty[b], 2 * (kGemmEpiThreads / 32));
     }
     mbar_init(done, 1);
+    for (int i = 0; i < 2 * (kGemmEpiThreads / 32); i++) mbar_init(&rfull[i], 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (TmaEpi<EPI>::kOn) tma_prefetch_desc(&tmC);
+    if constexpr (EPI == WX_EPI_F32_RESID) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, 2 * BN);
@@ -496,6 +605,76 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       umma_commit_pair(mapa_shared(smem_u32(done), 0));
       mbar_wait_for(done, 0, kWaitTimeoutNs);
     }
+  } else if constexpr (TmaEpi<EPI>::kOn) {
+    // ---------------- epilogue through shared memory + TMA stores: warps 2..9
+    constexpr int kCols = TmaEpi<EPI>::kCols, kChunks = (BN / 2) / kCols;
+    const int sub = warp & 3;          // TMEM lanes 32*sub .. 32*sub+31
+    const int half = (warp - 2) >> 2;  // column half of the tile
+    uint8_t* ebuf = sE + (warp - 2) * 2 * kEpiBufBytes;
+    uint64_t* rf = rfull + 2 * (warp - 2);
+    const int row_off = (int)rank * 128 + sub * 32;
+    // this warp's chunks of a tile: a prefix of kChunks (none past M or N)
+    auto chunks_of = [&](int tile) -> int {
+      const int r0 = (tile / nnb) * 256 + row_off, c0 = (tile % nnb) * BN + half * (BN / 2);
+      if (r0 >= a.M || c0 >= a.N) return 0;
+      return min(kChunks, (a.N - c0 + kCols - 1) / kCols);
+    };
+    // residual loads (lane 0) run two chunks ahead, across tiles
+    int lt = pair, lc = 0;
+    uint32_t lk = 0;
+    auto load_next = [&]() {
+      while (lt < a.num_tiles && lc >= chunks_of(lt)) { lt += npairs; lc = 0; }
+      if (lt >= a.num_tiles) return;
+      const uint32_t b = lk & 1;
+      mbar_arrive_expect_tx(&rf[b], kEpiBufBytes);
+      tma_load_2d(&tmR, &rf[b], ebuf + b * kEpiBufBytes,
+                  (lt % nnb) * BN + half * (BN / 2) + lc * kCols, (lt / nnb) * 256 + row_off);
+      lc++;
+      lk++;
+    };
+    if constexpr (EPI == WX_EPI_F32_RESID) {
+      if (lane == 0) { load_next(); load_next(); }
+    }
+    int acc = 0;
+    uint32_t acc_phase = 0, k = 0;
+    for (int tile = pair; ok && tile < a.num_tiles; tile += npairs) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, a.err));
+      if (!ok) break;
+      tc_fence_after();
+      const int nc = chunks_of(tile);
+      const int r0 = (tile / nnb) * 256 + row_off, c0 = (tile % nnb) * BN + half * (BN / 2);
+      const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16) +
+                             (uint32_t)(acc * BN + half * (BN / 2));
+      for (int c = 0; c < nc; c++, k++) {
+        uint8_t* buf = ebuf + (k & 1) * kEpiBufBytes;
+        if constexpr (EPI == WX_EPI_F32_RESID) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&rf[k & 1], (k >> 1) & 1, a.err));
+          if (!ok) break;
+        } else {
+          if (lane == 0) bulk_wait_group_read<1>();   // the store of chunk k-2 has read buf
+          __syncwarp();
+        }
+        epi_chunk_to_smem<EPI>(a, t_row + (uint32_t)(c * kCols), c0 + c * kCols,
+                               buf + lane * 128, lane);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, c0 + c * kCols, r0);
+          bulk_commit_group();
+          if constexpr (EPI == WX_EPI_F32_RESID) {
+            bulk_wait_group_read<0>();   // the store has read buf: refill it
+            load_next();
+          }
+        }
+      }
+      if (!ok) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    if (lane == 0) bulk_wait_group<0>();   // stores complete before the CTA retires
   } else {
     // ---------------- epilogue: warps 2..9 of both CTAs
     const int sub = warp & 3;          // TMEM lanes 32*sub .. 32*sub+31
@@ -560,6 +739,31 @@ static bool use_pair(int64_t M, int64_t N, int nsm) {
   return N > 128 && ((M + 255) / 256) * ((N + 255) / 256) >= nsm / 2;
 }
 
+// Tensor maps of the 2-SM kernel's TMA epilogue: C (and the residual) in
+// boxes of 32 rows x 128 bytes with the 128-byte swizzle; left zeroed for the
+// epilogues that store from registers.
+static int encode_epilogue_maps(GemmPlan* p, void* C, const float* R, int64_t M, int64_t N,
+                                int64_t ldc, int64_t ldr, int epi) {
+  memset(&p->tmC, 0, sizeof(p->tmC));
+  memset(&p->tmR, 0, sizeof(p->tmR));
+  const bool f32 = epi == WX_EPI_F32 || epi == WX_EPI_F32_RESID;
+  const bool bf16 = epi == WX_EPI_BF16 || epi == WX_EPI_BF16_GELU || epi == WX_EPI_BF16_GELU_ERF;
+  if (!p->pair || !(f32 || bf16)) return WX_OK;
+  if (f32)
+    WX_TRY(encode_tensor_map_2d(&p->tmC, C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)N,
+                                (uint64_t)M, (uint64_t)ldc * 4, 32, 32,
+                                CU_TENSOR_MAP_SWIZZLE_128B));
+  else
+    WX_TRY(encode_tensor_map_2d(&p->tmC, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)N,
+                                (uint64_t)M, (uint64_t)ldc * 2, 64, 32,
+                                CU_TENSOR_MAP_SWIZZLE_128B));
+  if (epi == WX_EPI_F32_RESID)
+    WX_TRY(encode_tensor_map_2d(&p->tmR, R, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)N,
+                                (uint64_t)M, (uint64_t)ldr * 4, 32, 32,
+                                CU_TENSOR_MAP_SWIZZLE_128B));
+  return WX_OK;
+}
+
 // Build the tensor maps and launch arguments once; the encoder keeps plans for
 // its fixed buffers, the standalone entry point builds one per call.
 int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, const float* R,
@@ -615,6 +819,7 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
   p->epi = epi;
   p->pair = pair;
   p->grid = pair ? 2 * std::min(g.num_tiles, nsm / 2) : std::min(g.num_tiles, nsm);
+  WX_TRY(encode_epilogue_maps(p, C, R, M, N, ldc, ldr, epi));
   return gemm_prepare(bn, epi, pair);
 }
 
@@ -667,6 +872,7 @@ int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, cons
   p->epi = epi;
   p->pair = pair;
   p->grid = pair ? 2 * std::min(g.num_tiles, nsm / 2) : std::min(g.num_tiles, nsm);
+  WX_TRY(encode_epilogue_maps(p, C, nullptr, M, N, ldc, 0, epi));
   return gemm_prepare(bn, epi, pair);
 }
 
@@ -689,7 +895,8 @@ static int set_attr_pair_t() {
   WX_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 64 && done[dev]) return WX_OK;
   WX_CUDA_TRY(cudaFuncSetAttribute(gemm2_bf16_kernel<EPI>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kGemm2Smem));
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Gemm2Cfg<EPI>::SMEM));
   if (dev < 64) done[dev] = true;
   return WX_OK;
 }
@@ -697,7 +904,8 @@ static int set_attr_pair_t() {
 template <int BN, int EPI>
 static int launch_t(const GemmPlan& p, cudaStream_t st) {
   if (p.pair) {
-    gemm2_bf16_kernel<EPI><<<p.grid, kGemmThreads, kGemm2Smem, st>>>(p.tmA, p.tmB, p.args);
+    gemm2_bf16_kernel<EPI><<<p.grid, kGemmThreads, Gemm2Cfg<EPI>::SMEM, st>>>(p.tmA, p.tmB, p.tmC,
+                                                                              p.tmR, p.args);
     return check_launch("gemm_bf16_pair");
   }
   gemm_bf16_kernel<BN, EPI><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, st>>>(p.tmA, p.tmB,

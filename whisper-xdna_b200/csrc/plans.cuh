@@ -26,6 +26,7 @@ constexpr int kEpiF32GeluErfPos = 17;  // GELU = exact erf form
 
 struct GemmPlan {
   CUtensorMap tmA, tmB;
+  CUtensorMap tmC, tmR;   // output / residual tiles of the 2-SM kernel's epilogue
   GemmArgs args;
   int bn;
   int grid;
