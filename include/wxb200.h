@@ -130,6 +130,40 @@ int wx_gemm_bf16(const void* A, const void* B, const float* bias, const float* R
                  int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                  int64_t ldr, int epilogue, void* stream);
 
+/* ------------------------------------------------------------ int8 */
+
+/* The reference's int8 projection/MLP mode (bench/probe_int8_decode.py:48-74,
+ * q_matmul_factory; README.md "int8 on the wide GEMMs"), on int8 tensor cores.
+ *
+ * wx_absmax_rows: out[r * out_stride] = max(out[r * out_stride], max_c |in[r, c]|)
+ * for r < rows (an atomic fold: out_stride 0 gives the maximum of the whole
+ * matrix, the "pertensor" weight scale). in is bf16 or fp32 (in_dtype), row
+ * stride ld_in elements. out must hold non-negative values (zero it first).
+ *
+ * wx_quantize_rows: per row r, m = rowmax[r * rowmax_stride] (or, with rowmax
+ * NULL, max_c |in[r, c]|); scale[r] = m / 127 (1 where that is 0);
+ * q[r, c] = rint(in[r, c] / scale[r]) as int8 (fp32 division rounded to
+ * nearest, integer rounding half to even: numpy's np.rint(A / sa)). Quantises
+ * activations per token and, applied to the torch weight (N, K), weights per
+ * output channel. q has row stride ld_q bytes.
+ *
+ * wx_gemm_i8: C = epilogue((float(A @ B^T) * sa[m]) * sw[n]) with A (M x K) and
+ * B (N x K) int8 row-major (lda, ldb multiples of 16, 16-byte aligned), s32
+ * accumulation (exact), sa (M) and sw (N, 16-byte aligned) fp32 scales; the
+ * two products are rounded separately, as (A_q @ B_q) * sa * sw in the
+ * reference. Epilogues as wx_gemm_bf16 (bias added after the scaling). rowmax
+ * (M floats, or NULL; bf16 epilogues only) receives max |C[m, :]| of the
+ * stored bf16 values by an atomic fold, for quantising C as the next GEMM's A. */
+int wx_absmax_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld_in,
+                   float* out, int64_t out_stride, void* stream);
+int wx_quantize_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld_in,
+                     const float* rowmax, int64_t rowmax_stride, int8_t* q, int64_t ld_q,
+                     float* scale, void* stream);
+int wx_gemm_i8(const int8_t* A, const int8_t* B, const float* sa, const float* sw,
+               const float* bias, const float* R, void* C, int64_t M, int64_t N, int64_t K,
+               int64_t lda, int64_t ldb, int64_t ldc, int64_t ldr, int epilogue, float* rowmax,
+               void* stream);
+
 /* ------------------------------------------------------------ attention */
 
 /* Fused attention, no mask: for every batch b < B and head h < H,
@@ -195,6 +229,20 @@ int wx_encoder_set_layer(wx_encoder* enc, int layer, const float* attn_ln_w,
                          const float* bo, const float* mlp_ln_w, const float* mlp_ln_b,
                          const float* w1, const float* b1, const float* w2, const float* b2);
 int wx_encoder_set_ln_post(wx_encoder* enc, const float* w, const float* b);
+
+/* int8 mode, the reference's int8 projection/MLP probe
+ * (bench/probe_int8_decode.py:48-74, its encoder call :140-142): the conv,
+ * QKV, out-proj, fc1 and fc2 GEMMs run on int8 operands (wx_gemm_i8), weights
+ * quantised once per output channel (PERCHAN) or per weight matrix
+ * (PERTENSOR: one scale for each of q, k, v, out, fc2, each conv, and each fc1
+ * column chunk of prepare_mlp_chunks, src/npu_whisper_encoder.py:383-398),
+ * activations per token right before each GEMM (wx_quantize_rows). Attention
+ * stays bf16. Call after wx_encoder_create and before any wx_encoder_set_*
+ * weight call; needs 3*n_mels, d_model and ffn multiples of 16. */
+#define WX_QUANT_NONE 0
+#define WX_QUANT_INT8_PERCHAN 1
+#define WX_QUANT_INT8_PERTENSOR 2
+int wx_encoder_set_quant(wx_encoder* enc, int mode);
 
 /* Forward on DEVICE buffers: mel (batch, n_mels, n_frames) fp32 ->
  * out (batch, n_frames / 2, d_model) fp32. n_frames even, n_frames / 2 <= n_ctx

@@ -27,6 +27,8 @@ biases ~ N(0, 0.02) rounded to bf16, LayerNorm gamma = 1 and beta = 0,
 sinusoidal positions, log-mel ~ U[-0.8, 1.2]; the recipe of
 bench/run_raw_block.py:71-92 and the build's BASELINE configs.
 """
+import math
+
 import numpy as np
 
 from rowops_ref import rbf, RNE
@@ -135,8 +137,9 @@ def _erf(x):
 
 
 def gelu_np(x):
-    """src/npu_whisper_encoder.py:284-287."""
-    return 0.5 * x * (1.0 + _erf(x / np.sqrt(2.0)))
+    """src/npu_whisper_encoder.py:284-287. The divisor is a Python float
+    (math.sqrt there), so float32 input stays float32 as in the reference."""
+    return 0.5 * x * (1.0 + _erf(x / math.sqrt(2.0)))
 
 
 def layer_norm_np(x, w, b, eps=1e-5):

@@ -1,0 +1,190 @@
+"""int8 mode on the GPU against the int8 oracle (oracle/quant_ref.py), which is
+pinned to the reference's own q_matmul_factory and encoder
+(bench/probe_int8_decode.py:48-74, :140-142).
+
+Bit-exact: the row quantiser, the int8 GEMM with its dequantising epilogues,
+and the device q_matmul (quantise -> int8 GEMM -> scale) against the
+reference's outputs. Tolerance: the int8 encoder against the reference's int8
+encoder, whose attention runs in fp32 where this one runs bf16.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import encoder_ref as R
+import quant_ref as Q
+import rowops_ref as O
+from wxb200 import _lib as L
+from wxb200 import ops
+from wxb200.encoder import Encoder
+from wxb200.quant import q_matmul_factory
+
+from test_quant_oracle import enc_case, gemm_inputs
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+def bf16_to_f32(t):
+    return (t.cpu().view(torch.int16).numpy().view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def rand_i8(shape, seed):
+    g = np.random.default_rng(seed)
+    return g.integers(-127, 128, size=shape, dtype=np.int64).astype(np.int8)
+
+
+def pad16(q):
+    """int8 (rows, cols) numpy -> CUDA int8 view with rows 16-byte aligned."""
+    rows, cols = q.shape
+    buf = torch.zeros(rows, (cols + 15) // 16 * 16, dtype=torch.int8)
+    buf[:, :cols] = torch.from_numpy(q)
+    return buf.cuda()[:, :cols]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,cols", [(64, 256), (37, 203), (5, 5120), (300, 1280)])
+def test_quantize_rows_matches_numpy(cuda, dtype, rows, cols):
+    g = torch.Generator().manual_seed(rows + cols)
+    x = (torch.randn(rows, cols, generator=g) * torch.rand(rows, 1, generator=g) * 4).to(dtype)
+    x[rows // 2] = 0                       # zero row: scale 1
+    q, s = ops.quantize_rows(x.cuda())
+    xf = x.float().numpy()
+    rq, rs = Q.quantize_rows(xf)
+    assert np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(q.cpu().numpy(), rq)
+
+
+def test_quantize_rows_given_maxima(cuda):
+    x = torch.randn(40, 96, generator=torch.Generator().manual_seed(3)).cuda()
+    m = ops.absmax_rows(x)
+    assert np.array_equal(m.cpu().numpy(), x.abs().max(dim=1).values.cpu().numpy())
+    q1, s1 = ops.quantize_rows(x, rowmax=m)
+    q0, s0 = ops.quantize_rows(x)
+    assert torch.equal(q0, q1) and torch.equal(s0, s1)
+    gm = ops.absmax_rows(x, per_row=False)          # one value for all rows
+    assert gm.item() == x.abs().max().item()
+    q2, s2 = ops.quantize_rows(x, rowmax=gm)
+    rq = np.rint(x.cpu().numpy() / (np.float32(gm.item()) / np.float32(127))).astype(np.int8)
+    assert np.array_equal(q2.cpu().numpy(), rq)
+    assert np.all(s2.cpu().numpy() == np.float32(gm.item()) / np.float32(127))
+
+
+def ref_gemm_i8(qa, qw, sa, sw, bias=None):
+    r = (qa.astype(np.float64) @ qw.astype(np.float64).T).astype(np.float32)
+    r = r * sa[:, None] * sw[None, :]
+    return r if bias is None else r + bias
+
+
+# single-CTA tiles, a K tail, and shapes that take the CTA-pair kernel
+SHAPES = [(200, 136, 200), (1500, 384, 1536), (4096, 1280, 1280), (3000, 5120, 1280)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_i8_f32_exact(cuda, M, N, K):
+    qa, qw = rand_i8((M, K), M), rand_i8((N, K), N)
+    g = np.random.default_rng(K)
+    sa = (g.random(M) * 0.01 + 1e-4).astype(np.float32)
+    sw = (g.random(N) * 0.001 + 1e-5).astype(np.float32)
+    bias = g.standard_normal(N).astype(np.float32)
+    out = ops.gemm_i8(pad16(qa), pad16(qw), torch.from_numpy(sa).cuda(),
+                      torch.from_numpy(sw).cuda(), bias=torch.from_numpy(bias).cuda())
+    assert np.array_equal(out.cpu().numpy(), ref_gemm_i8(qa, qw, sa, sw, bias))
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_i8_epilogues(cuda, M, N, K):
+    """Residual, bf16 and GELU epilogues: the same fp32 values as the F32
+    epilogue, then the bf16 path's rounding / g4f; rowmax = max |stored row|."""
+    qa, qw = pad16(rand_i8((M, K), M + 1)), pad16(rand_i8((N, K), N + 1))
+    g = torch.Generator().manual_seed(5)
+    sa = (torch.rand(M, generator=g) * 0.01).cuda()
+    sw = (torch.rand(N, generator=g) * 0.001).cuda()
+    bias = torch.randn(N, generator=g).cuda()
+    acc = ops.gemm_i8(qa, qw, sa, sw, bias=bias)
+    x = torch.randn(M, N, generator=g).cuda()
+    want = (acc + x).cpu().numpy()
+    ops.gemm_i8(qa, qw, sa, sw, bias=bias, residual=x, out=x, epilogue=L.WX_EPI_F32_RESID)
+    assert np.array_equal(x.cpu().numpy(), want)
+    b16 = ops.gemm_i8(qa, qw, sa, sw, bias=bias, epilogue=L.WX_EPI_BF16)
+    assert torch.equal(b16, acc.to(torch.bfloat16))
+    rowmax = torch.zeros(M, device="cuda")
+    gl = ops.gemm_i8(qa, qw, sa, sw, bias=bias, epilogue=L.WX_EPI_BF16_GELU, rowmax=rowmax)
+    gf = bf16_to_f32(gl)
+    assert np.array_equal(gf, O.gelu_row4f(acc.cpu().numpy()))
+    assert np.array_equal(rowmax.cpu().numpy(), np.abs(gf).max(axis=1))
+
+
+@pytest.mark.parametrize("mode", ["perchan", "pertensor"])
+def test_q_matmul_equals_reference(cuda, mode):
+    """The device q_matmul on the fixture inputs equals the output of the
+    reference's own q_matmul_factory bit for bit."""
+    z = np.load(GOLD / "quant_gemm.npz")
+    qm = q_matmul_factory(mode)
+    for i, (M, K, N) in enumerate(z["shapes"]):
+        A, B, bias = gemm_inputs(int(M), int(K), int(N), seed=100 + i)
+        out = qm(A, B, bias=bias)
+        assert out.dtype == np.float32 and np.array_equal(out, z[f"s{i}_{mode}"]), (i, mode)
+
+
+def test_q_matmul_fp32_control(cuda):
+    z = np.load(GOLD / "quant_gemm.npz")
+    A, B, bias = gemm_inputs(*[int(v) for v in z["shapes"][0]], seed=100)
+    out = q_matmul_factory("fp32")(A, B, bias=bias)
+    assert np.allclose(out, z["s0_fp32"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["tiny_l2_ctx64_perchan", "tiny_l2_ctx64_pertensor",
+                                  "large_l1_ctx32_perchan", "large_l1_ctx32_pertensor"])
+def test_int8_encoder_vs_reference(cuda, name):
+    """Encoder(quant="int8-...", gelu="erf") against the reference encoder run
+    with its int8 matmul. The reference keeps attention in fp32 and quantises
+    fp32 activations; here attention and the activations it quantises are bf16,
+    which moves values across rounding boundaries of the quantiser, so the
+    comparison is by cosine: >= 0.999 at these depths (the reference's own
+    int8 encoder is at 0.78-0.93 against fp32 at large-v3 depth, README.md
+    "int8 on the wide GEMMs")."""
+    W, mel, nl, nh, mode, ref = enc_case(name)
+    enc = Encoder(W, n_layer=nl, n_head=nh, gelu="erf", quant="int8-" + mode)
+    try:
+        out = enc.forward_host(mel)
+    finally:
+        enc.close()
+    assert out.shape == ref.shape
+    assert R.cosine(out, ref) >= 0.999, R.cosine(out, ref)
+    assert L.device_error() == 0
+
+
+def test_int8_encoder_graph_replay_and_batch(cuda):
+    W = R.make_weights("tiny", seed=4, n_layer=2)
+    mels = np.stack([R.make_mel(80, 256, seed=20 + i) for i in range(3)])
+    enc = Encoder(W, n_layer=2, n_head=6, gelu="erf", quant="int8-perchan", max_batch=3)
+    try:
+        a = enc.forward_host(mels, use_graph=True)
+        b = enc.forward_host(mels, use_graph=True)
+        c = enc.forward_host(mels, use_graph=False)
+        assert np.array_equal(a, b) and np.array_equal(a, c)
+        for i in range(3):
+            assert np.array_equal(enc.forward_host(mels[i]), a[i])
+    finally:
+        enc.close()
+
+
+def test_set_quant_rules(cuda):
+    W = R.make_weights("tiny", seed=4, n_layer=1)
+    enc = Encoder(W, n_layer=1, n_head=6)          # weights already set
+    try:
+        with pytest.raises(ValueError, match="before any weights"):
+            L.check(L.lib().wx_encoder_set_quant(enc._h, L.WX_QUANT_INT8_PERCHAN))
+        with pytest.raises(ValueError, match="mode 7"):
+            L.check(L.lib().wx_encoder_set_quant(enc._h, 7))
+    finally:
+        enc.close()
+    with pytest.raises(ValueError):
+        Encoder(W, n_layer=1, n_head=6, quant="int4")
+
+
+def test_no_device_error_recorded(cuda):
+    assert L.device_error() == 0

@@ -386,20 +386,23 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       const float m_use = grow ? mx : m;
       const float corr = fast_exp2(m - m_use);        // 1 when m stays, 0 on block 0
       m = m_use;
-      float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent accumulators
-      const float negm = -m;
+      // packed fp32 pairs (fma/add .f32x2): one instruction for two elements
+      float2 sums[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+      const float2 c2 = make_float2(c, c), negm2 = make_float2(-m, -m);
       uint32_t pw[kAttHalf / 2];
       auto make_p = [&](auto masked) {
 #pragma unroll
         for (int i = 0; i < kAttHalf; i += 2) {
-          float p0 = fast_exp2(fmaf(__uint_as_float(s[i]), c, negm));
-          float p1 = fast_exp2(fmaf(__uint_as_float(s[i + 1]), c, negm));
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[i]), __uint_as_float(s[i + 1])),
+                                      c2, negm2);
+          float p0 = fast_exp2(x.x);
+          float p1 = fast_exp2(x.y);
           if (decltype(masked)::value) {
             p0 = (i < kvalid) ? p0 : 0.0f;
             p1 = (i + 1 < kvalid) ? p1 : 0.0f;
           }
           pw[i / 2] = pack_bf16x2_rne(p0, p1);
-          sums[(i / 2) & 3] += p0 + p1;
+          sums[(i / 2) & 1] = __fadd2_rn(sums[(i / 2) & 1], make_float2(p0, p1));
         }
       };
       // SFU turns (seq): tile A's exponentials of block j wait for tile B's of
@@ -425,14 +428,20 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         uint32_t ov[32];
         tmem_ld32(t_o, ov);
         tmem_wait_ld();
+        const float2 corr2 = make_float2(corr, corr);
 #pragma unroll
-        for (int i = 0; i < 32; i++) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
+        for (int i = 0; i < 32; i += 2) {
+          const float2 o2 = __fmul2_rn(make_float2(__uint_as_float(ov[i]), __uint_as_float(ov[i + 1])),
+                                       corr2);
+          ov[i] = __float_as_uint(o2.x);
+          ov[i + 1] = __float_as_uint(o2.y);
+        }
         tmem_st32(t_o, ov);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[2 * t + (j & 1)]);
-      l = l * corr + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
+      l = l * corr + ((sums[0].x + sums[1].x) + (sums[0].y + sums[1].y));
     }
     // tile B's last turn is consumed, so no phase is left pending at exit
     if (t == 0 && !mbar_wait(&seq[4 + sub], (uint32_t)(nkv - 1) & 1u, a.err)) ok = false;

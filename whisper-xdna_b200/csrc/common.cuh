@@ -436,6 +436,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn_maj
          ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor, kind::i8: s32 accumulator (bits 4-5 = 2), signed
+// 8-bit A and B (bits 7-9, 10-12 = 1), both K-major, N >> 3, M >> 4.
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 

@@ -16,6 +16,17 @@
 //   ln_post (fp32 out)                   :538
 // The reference's q * hd^-0.25 and k * hd^-0.25 scaling becomes one 1/sqrt(hd)
 // on the scores inside the attention kernel.
+//
+// int8 mode (wx_encoder_set_quant; the reference's int8 probe,
+// bench/probe_int8_decode.py:48-74 with :140-142): the conv, QKV, out-proj,
+// fc1 and fc2 GEMMs take int8 operands on the int8 tensor cores. Weights are
+// quantised once per output channel (or per weight matrix, per q/k/v and per
+// fc1 column chunk of prepare_mlp_chunks for "pertensor"); each GEMM's
+// activation rows are quantised per token right before it:
+//   im2col (bf16) -> quantise -> conv GEMM          LN (fp32) -> quantise -> QKV
+//   attention (bf16) -> quantise -> out-proj          LN (fp32) -> quantise -> fc1
+//   fc1 + GELU (bf16, with max |row| by atomics) -> quantise -> fc2
+// Attention itself stays bf16 (the probe keeps it in fp32: E.np_matmul).
 #include <algorithm>
 #include <map>
 #include <mutex>
@@ -43,6 +54,18 @@ __global__ void convert_bf16_kernel(const float* __restrict__ src, uint16_t* __r
       si = o * 3 * conv_C + c * 3 + j;
     }
     dst[i] = (uint16_t)bf16_bits<RND_RNE>(src[si]);
+  }
+}
+
+// fp32 copy with the same optional conv2 column permutation (int8 weights are
+// quantised from the permuted fp32 matrix)
+__global__ void permute_f32_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                   int64_t n, int conv_C) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = i / (3 * conv_C), rem = i % (3 * conv_C);
+    const int64_t j = rem / conv_C, c = rem % conv_C;
+    dst[i] = src[o * 3 * conv_C + c * 3 + j];
   }
 }
 
@@ -102,6 +125,9 @@ struct LayerW {
   uint16_t *wqkv, *wo, *w1, *w2;                    // bf16, (out, in)
   float *bqkv, *bo, *b1, *b2;                       // fp32
   float *ln1_g, *ln1_b, *ln2_g, *ln2_b;             // fp32
+  // int8 mode: the same weights quantised per output channel, and the scales
+  int8_t *qqkv = nullptr, *qo = nullptr, *q1 = nullptr, *q2 = nullptr;
+  float *sqkv = nullptr, *so = nullptr, *s1 = nullptr, *s2 = nullptr;
 };
 
 struct Plans {
@@ -141,7 +167,17 @@ struct wx_encoder {
   float* mel_dev = nullptr;   // (B, n_mels, 2*n_ctx) staging for host input
   float* out_dev = nullptr;   // (B, n_ctx, d) staging for host output
   float* stage = nullptr;     // fp32 upload staging for weights
+  float* stage2 = nullptr;    // int8 mode: permuted fp32 weights
   int64_t stage_n = 0;
+  // int8 mode (WX_QUANT_*)
+  int quant = 0;
+  int8_t *conv1_q = nullptr, *conv2_q = nullptr;
+  float *conv1_s = nullptr, *conv2_s = nullptr;
+  int8_t* aq = nullptr;       // (B*T, d) int8: the quantised LN / attention output
+  int8_t* fq = nullptr;       // int8 fc1 output (B*T, ffn) and conv im2col rows
+  float* sa = nullptr;        // per-row scales of aq / fq (2*B*T)
+  float* rowmax = nullptr;    // (B*T) max |fc1 output| per row
+  float* gmax = nullptr;      // one weight matrix's max |w| ("pertensor")
   bool set_front = false, set_post = false;
   std::vector<bool> set_layer;
   std::map<std::pair<int64_t, int64_t>, wx::Plans*> plans;
@@ -185,6 +221,46 @@ static int upload_bf16(wx_encoder* e, uint16_t* dst, const float* src, int64_t n
   return WX_OK;
 }
 
+// int8 mode: quantise a weight (rows x cols fp32 on the host, conv_C > 0 for
+// the conv2 column permutation) into dst with one scale per row (output
+// channel). "pertensor" uses one scale per group of group_rows rows: the
+// whole matrix, or one of q / k / v, or one fc1 column chunk.
+static int upload_i8(wx_encoder* e, int8_t* dst, float* scale, const float* src, int64_t rows,
+                     int64_t cols, int conv_C, int64_t group_rows) {
+  if (!src) return fail(WX_ERR_INVALID, "encoder: NULL weight pointer");
+  const int64_t n = rows * cols;
+  if (n > e->stage_n) return fail(WX_ERR_INVALID, "encoder: staging too small");
+  WX_CUDA_TRY(cudaMemcpy(e->stage, src, (size_t)n * 4, cudaMemcpyHostToDevice));
+  const float* w = e->stage;
+  if (conv_C > 0) {
+    permute_f32_kernel<<<1024, 256>>>(e->stage, e->stage2, n, conv_C);
+    WX_TRY(check_launch("permute_f32"));
+    w = e->stage2;
+  }
+  if (e->quant == WX_QUANT_INT8_PERCHAN) {
+    WX_TRY(launch_quantize_rows(w, WX_DTYPE_F32, rows, cols, cols, nullptr, 0, dst, cols, scale, 0));
+  } else {
+    for (int64_t g = 0; g < rows; g += group_rows) {
+      const int64_t gr = std::min(group_rows, rows - g);
+      WX_CUDA_TRY(cudaMemset(e->gmax, 0, 4));
+      WX_TRY(launch_absmax_rows(w + g * cols, WX_DTYPE_F32, gr, cols, cols, e->gmax, 0, 0));
+      WX_TRY(launch_quantize_rows(w + g * cols, WX_DTYPE_F32, gr, cols, cols, e->gmax, 0,
+                                  dst + g * cols, cols, scale + g, 0));
+    }
+  }
+  WX_CUDA_TRY(cudaDeviceSynchronize());
+  return WX_OK;
+}
+
+// fc1's column chunk in the reference's prepare_mlp_chunks(W, n_layer, d, 0)
+// (src/npu_whisper_encoder.py:383-398): the whole width up to 4096, else d
+// when d divides it, else an even split.
+static int64_t fc1_chunk(int64_t ffn, int64_t d) {
+  if (ffn <= 4096) return ffn;
+  if (ffn % d == 0) return d;
+  return ffn / ((ffn + 4095) / 4096);
+}
+
 static int build_plans(wx_encoder* e, int64_t B, int64_t T, Plans** out) {
   auto it = e->plans.find({B, T});
   if (it != e->plans.end()) {
@@ -197,20 +273,49 @@ static int build_plans(wx_encoder* e, int64_t B, int64_t T, Plans** out) {
   const int gelu_bf16 = e->gelu_mode == WX_GELU_ERF ? WX_EPI_BF16_GELU_ERF : WX_EPI_BF16_GELU;
   const int gelu_pos = e->gelu_mode == WX_GELU_ERF ? kEpiF32GeluErfPos : kEpiF32GeluPos;
   int s = WX_OK;
+  if (e->quant) {
+    // int8 GEMMs: conv inputs quantised into fq, LN / attention outputs into aq
+    s = gemm_plan_i8(&p->conv1, e->fq, e->conv1_q, e->sa, e->conv1_s, e->conv1_b, nullptr, e->qkv,
+                     B * F2, d, K1, K1, K1, d, 0, gelu_bf16, nullptr);
+    if (s == WX_OK)
+      s = gemm_plan_i8(&p->conv2, e->fq, e->conv2_q, e->sa, e->conv2_s, e->conv2_b, nullptr, e->x,
+                       M, d, 3 * d, 3 * d, 3 * d, d, 0, gelu_pos, nullptr);
+    if (s == WX_OK) gemm_set_pos(&p->conv2, e->pos, d, (int)T);
+    p->qkv.resize(e->nl);
+    p->out.resize(e->nl);
+    p->fc1.resize(e->nl);
+    p->fc2.resize(e->nl);
+    for (int l = 0; s == WX_OK && l < e->nl; l++) {
+      const LayerW& w = e->L[l];
+      s = gemm_plan_i8(&p->qkv[l], e->aq, w.qqkv, e->sa, w.sqkv, w.bqkv, nullptr, e->qkv, M, 3 * d,
+                       d, d, d, 3 * d, 0, WX_EPI_BF16, nullptr);
+      if (s == WX_OK)
+        s = gemm_plan_i8(&p->out[l], e->aq, w.qo, e->sa, w.so, w.bo, e->x, e->x, M, d, d, d, d, d,
+                         d, WX_EPI_F32_RESID, nullptr);
+      if (s == WX_OK)
+        s = gemm_plan_i8(&p->fc1[l], e->aq, w.q1, e->sa, w.s1, w.b1, nullptr, e->f, M, ffn, d, d, d,
+                         ffn, 0, gelu_bf16, e->rowmax);
+      if (s == WX_OK)
+        s = gemm_plan_i8(&p->fc2[l], e->fq, w.q2, e->sa, w.s2, w.b2, e->x, e->x, M, d, ffn, ffn, ffn,
+                         d, d, WX_EPI_F32_RESID, nullptr);
+    }
+  }
   // conv1: A1 (B*2T, 3*n_mels) in f, out x1 (B*2T, d) in qkv
-  if (s == WX_OK)
+  if (s == WX_OK && !e->quant)
     s = gemm_plan(&p->conv1, e->f, e->conv1_w, e->conv1_b, nullptr, e->qkv, B * F2, d, K1, K1, K1,
                   d, 0, gelu_bf16, 0);
   // conv2: A2 (B*T, 3d) in f, out x fp32 (+ positions)
-  if (s == WX_OK)
+  if (s == WX_OK && !e->quant)
     s = gemm_plan(&p->conv2, e->f, e->conv2_w, e->conv2_b, nullptr, e->x, M, d, 3 * d, 3 * d,
                   3 * d, d, 0, gelu_pos, 0);
-  if (s == WX_OK) gemm_set_pos(&p->conv2, e->pos, d, (int)T);
-  p->qkv.resize(e->nl);
-  p->out.resize(e->nl);
-  p->fc1.resize(e->nl);
-  p->fc2.resize(e->nl);
-  for (int l = 0; s == WX_OK && l < e->nl; l++) {
+  if (s == WX_OK && !e->quant) gemm_set_pos(&p->conv2, e->pos, d, (int)T);
+  if (!e->quant) {
+    p->qkv.resize(e->nl);
+    p->out.resize(e->nl);
+    p->fc1.resize(e->nl);
+    p->fc2.resize(e->nl);
+  }
+  for (int l = 0; s == WX_OK && !e->quant && l < e->nl; l++) {
     const LayerW& w = e->L[l];
     s = gemm_plan(&p->qkv[l], e->h, w.wqkv, w.bqkv, nullptr, e->qkv, M, 3 * d, d, d, d, 3 * d, 0,
                   WX_EPI_BF16, 0);
@@ -236,9 +341,55 @@ static int build_plans(wx_encoder* e, int64_t B, int64_t T, Plans** out) {
   return WX_OK;
 }
 
+// The launch sequence of one int8-mode forward pass.
+static int forward_launches_i8(wx_encoder* e, Plans* p, const float* mel, float* out, int64_t B,
+                               int64_t T, cudaStream_t st) {
+  const int64_t M = B * T, F2 = 2 * T, d = e->d, ffn = e->ffn, K1 = 3 * (int64_t)e->n_mels;
+  float* h32 = reinterpret_cast<float*>(e->f);   // fp32 LN output (f holds M*ffn bf16)
+  {
+    const size_t smem = (size_t)e->n_mels * 34 * 4;
+    dim3 grid((unsigned)((F2 + 31) / 32), (unsigned)B);
+    im2col_conv1_kernel<<<grid, 256, smem, st>>>(mel, e->f, e->n_mels, (int)F2);
+    WX_TRY(check_launch("im2col_conv1"));
+  }
+  WX_TRY(launch_quantize_rows(e->f, WX_DTYPE_BF16, B * F2, K1, K1, nullptr, 0, e->fq, K1, e->sa, st));
+  WX_TRY(gemm_run(p->conv1, st));
+  {
+    const int64_t total = M * (3 * d / 8);
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 8);
+    im2col_conv2_kernel<<<grid, 256, 0, st>>>(e->qkv, e->f, M, (int)T, (int)d);
+    WX_TRY(check_launch("im2col_conv2"));
+  }
+  WX_TRY(launch_quantize_rows(e->f, WX_DTYPE_BF16, M, 3 * d, 3 * d, nullptr, 0, e->fq, 3 * d, e->sa,
+                              st));
+  WX_TRY(gemm_run(p->conv2, st));
+  for (int l = 0; l < e->nl; l++) {
+    const LayerW& w = e->L[l];
+    WX_TRY(launch_layernorm_rows(e->x, WX_DTYPE_F32, w.ln1_g, w.ln1_b, h32, WX_DTYPE_F32, M, d, d,
+                                 d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st));
+    WX_TRY(launch_quantize_rows(h32, WX_DTYPE_F32, M, d, d, nullptr, 0, e->aq, d, e->sa, st));
+    WX_TRY(gemm_run(p->qkv[l], st));
+    WX_TRY(attn_run(p->attn, st));
+    WX_TRY(launch_quantize_rows(e->o, WX_DTYPE_BF16, M, d, d, nullptr, 0, e->aq, d, e->sa, st));
+    WX_TRY(gemm_run(p->out[l], st));
+    WX_TRY(launch_layernorm_rows(e->x, WX_DTYPE_F32, w.ln2_g, w.ln2_b, h32, WX_DTYPE_F32, M, d, d,
+                                 d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st));
+    WX_TRY(launch_quantize_rows(h32, WX_DTYPE_F32, M, d, d, nullptr, 0, e->aq, d, e->sa, st));
+    WX_CUDA_TRY(cudaMemsetAsync(e->rowmax, 0, (size_t)M * 4, st));
+    WX_TRY(gemm_run(p->fc1[l], st));
+    WX_TRY(launch_quantize_rows(e->f, WX_DTYPE_BF16, M, ffn, ffn, e->rowmax, 1, e->fq, ffn, e->sa,
+                                st));
+    WX_TRY(gemm_run(p->fc2[l], st));
+  }
+  WX_TRY(launch_layernorm_rows(e->x, WX_DTYPE_F32, e->lnp_g, e->lnp_b, out, WX_DTYPE_F32, M, d, d,
+                               d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st));
+  return WX_OK;
+}
+
 // The launch sequence of one forward pass.
 static int forward_launches(wx_encoder* e, Plans* p, const float* mel, float* out, int64_t B,
                             int64_t T, cudaStream_t st) {
+  if (e->quant) return forward_launches_i8(e, p, mel, out, B, T, st);
   const int64_t M = B * T, F2 = 2 * T, d = e->d;
   {
     const size_t smem = (size_t)e->n_mels * 34 * 4;
@@ -383,8 +534,14 @@ int wx_encoder_set_frontend(wx_encoder* e, const float* conv1_w, const float* co
                             const float* conv2_w, const float* conv2_b, const float* pos) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
   const int64_t d = e->d;
-  WX_TRY(upload_bf16(e, e->conv1_w, conv1_w, d * 3 * e->n_mels, 0));
-  WX_TRY(upload_bf16(e, e->conv2_w, conv2_w, d * 3 * d, (int)d));
+  if (e->quant) {
+    const int64_t k1 = 3 * (int64_t)e->n_mels;
+    WX_TRY(upload_i8(e, e->conv1_q, e->conv1_s, conv1_w, d, k1, 0, d));
+    WX_TRY(upload_i8(e, e->conv2_q, e->conv2_s, conv2_w, d, 3 * d, (int)d, d));
+  } else {
+    WX_TRY(upload_bf16(e, e->conv1_w, conv1_w, d * 3 * e->n_mels, 0));
+    WX_TRY(upload_bf16(e, e->conv2_w, conv2_w, d * 3 * d, (int)d));
+  }
   WX_TRY(upload_f32(e, e->conv1_b, conv1_b, d));
   WX_TRY(upload_f32(e, e->conv2_b, conv2_b, d));
   WX_TRY(upload_f32(e, e->pos, pos, (int64_t)e->n_ctx * d));
@@ -401,12 +558,21 @@ int wx_encoder_set_layer(wx_encoder* e, int layer, const float* attn_ln_w, const
   if (layer < 0 || layer >= e->nl) return fail(WX_ERR_INVALID, "encoder: layer %d", layer);
   const int64_t d = e->d, ffn = e->ffn;
   LayerW& w = e->L[layer];
-  WX_TRY(upload_bf16(e, w.wqkv, wq, d * d, 0));
-  WX_TRY(upload_bf16(e, w.wqkv + d * d, wk, d * d, 0));
-  WX_TRY(upload_bf16(e, w.wqkv + 2 * d * d, wv, d * d, 0));
-  WX_TRY(upload_bf16(e, w.wo, wo, d * d, 0));
-  WX_TRY(upload_bf16(e, w.w1, w1, ffn * d, 0));
-  WX_TRY(upload_bf16(e, w.w2, w2, ffn * d, 0));
+  if (e->quant) {
+    WX_TRY(upload_i8(e, w.qqkv, w.sqkv, wq, d, d, 0, d));
+    WX_TRY(upload_i8(e, w.qqkv + d * d, w.sqkv + d, wk, d, d, 0, d));
+    WX_TRY(upload_i8(e, w.qqkv + 2 * d * d, w.sqkv + 2 * d, wv, d, d, 0, d));
+    WX_TRY(upload_i8(e, w.qo, w.so, wo, d, d, 0, d));
+    WX_TRY(upload_i8(e, w.q1, w.s1, w1, ffn, d, 0, fc1_chunk(ffn, d)));
+    WX_TRY(upload_i8(e, w.q2, w.s2, w2, d, ffn, 0, d));
+  } else {
+    WX_TRY(upload_bf16(e, w.wqkv, wq, d * d, 0));
+    WX_TRY(upload_bf16(e, w.wqkv + d * d, wk, d * d, 0));
+    WX_TRY(upload_bf16(e, w.wqkv + 2 * d * d, wv, d * d, 0));
+    WX_TRY(upload_bf16(e, w.wo, wo, d * d, 0));
+    WX_TRY(upload_bf16(e, w.w1, w1, ffn * d, 0));
+    WX_TRY(upload_bf16(e, w.w2, w2, ffn * d, 0));
+  }
   WX_TRY(upload_f32(e, w.bqkv, bq, d));
   WX_CUDA_TRY(cudaMemset(w.bqkv + d, 0, d * 4));  // the key projection has no bias
   WX_TRY(upload_f32(e, w.bqkv + 2 * d, bv, d));
@@ -418,6 +584,47 @@ int wx_encoder_set_layer(wx_encoder* e, int layer, const float* attn_ln_w, const
   WX_TRY(upload_f32(e, w.ln2_g, mlp_ln_w, d));
   WX_TRY(upload_f32(e, w.ln2_b, mlp_ln_b, d));
   e->set_layer[layer] = true;
+  return WX_OK;
+}
+
+int wx_encoder_set_quant(wx_encoder* e, int mode) {
+  if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  if (mode != WX_QUANT_NONE && mode != WX_QUANT_INT8_PERCHAN && mode != WX_QUANT_INT8_PERTENSOR)
+    return fail(WX_ERR_INVALID, "encoder_set_quant: mode %d", mode);
+  if (e->set_front || e->set_post || std::find(e->set_layer.begin(), e->set_layer.end(), true) !=
+                                         e->set_layer.end())
+    return fail(WX_ERR_INVALID, "encoder_set_quant: call before any weights are set");
+  if (e->quant != WX_QUANT_NONE && mode != e->quant)
+    return fail(WX_ERR_INVALID, "encoder_set_quant: the mode is already set");
+  if (mode == WX_QUANT_NONE || e->quant == mode) return WX_OK;
+  const int64_t d = e->d, ffn = e->ffn, B = e->max_batch, T = e->n_ctx, M = B * T;
+  const int64_t k1 = 3 * (int64_t)e->n_mels;
+  if (k1 % 16 || d % 16 || ffn % 16)
+    return fail(WX_ERR_UNSUPPORTED, "encoder_set_quant: 3*n_mels, d and ffn must be multiples of 16");
+  int s = WX_OK;
+  auto A = [&](void** p, int64_t bytes) { if (s == WX_OK) s = dalloc(e, p, bytes); };
+  A((void**)&e->conv1_q, d * k1);
+  A((void**)&e->conv2_q, d * 3 * d);
+  A((void**)&e->conv1_s, d * 4);
+  A((void**)&e->conv2_s, d * 4);
+  for (LayerW& w : e->L) {
+    A((void**)&w.qqkv, 3 * d * d);
+    A((void**)&w.qo, d * d);
+    A((void**)&w.q1, ffn * d);
+    A((void**)&w.q2, ffn * d);
+    A((void**)&w.sqkv, 3 * d * 4);
+    A((void**)&w.so, d * 4);
+    A((void**)&w.s1, ffn * 4);
+    A((void**)&w.s2, d * 4);
+  }
+  A((void**)&e->aq, M * d);
+  A((void**)&e->fq, std::max(M * ffn, std::max(B * 2 * T * k1, M * 3 * d)));
+  A((void**)&e->sa, 2 * M * 4);
+  A((void**)&e->rowmax, M * 4);
+  A((void**)&e->gmax, 16);
+  A((void**)&e->stage2, e->stage_n * 4);
+  if (s != WX_OK) return s;   // the allocations made are released with the encoder
+  e->quant = mode;
   return WX_OK;
 }
 

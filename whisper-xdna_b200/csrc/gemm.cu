@@ -47,15 +47,60 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
+// int8 GEMM: accumulator columns n..n+31 of one row as fp32,
+// (float(acc) * sa[row]) * sw[col], each product rounded on its own (the order
+// of the reference's (A_q @ B_q) * sa * sw in fp32).
+__device__ __forceinline__ void dequant32(const GemmArgs& a, float s_row, int n,
+                                          const uint32_t (&acc)[32], float (&v)[32]) {
+  if (n + 32 <= a.N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(a.sw + n + j));
+      v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j]), s_row), w.x);
+      v[j + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j + 1]), s_row), w.y);
+      v[j + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j + 2]), s_row), w.z);
+      v[j + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j + 3]), s_row), w.w);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      v[j] = n + j < a.N ? __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j]), s_row), a.sw[n + j])
+                         : 0.0f;
+  }
+}
+
+// max |x| over the bf16 pairs w[0..npairs) whose columns lie below `valid`
+// (column 2i in the low half), as bf16 magnitude bits
+template <int NP>
+__device__ __forceinline__ uint32_t absmax_bf16x2(const uint32_t (&w)[NP], int valid) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < NP; i++) {
+    const uint32_t lo = 2 * i < valid ? (w[i] & 0x7FFFu) : 0u;
+    const uint32_t hi = 2 * i + 1 < valid ? ((w[i] >> 16) & 0x7FFFu) : 0u;
+    m = max(m, max(lo, hi));
+  }
+  return m;
+}
+// fold a bf16 magnitude into rowmax[row] (fp32 bits of non-negative values
+// order like unsigned integers)
+__device__ __forceinline__ void rowmax_update(float* rowmax, int row, uint32_t bf16_mag) {
+  if (bf16_mag) atomicMax(reinterpret_cast<unsigned int*>(rowmax) + row, bf16_mag << 16);
+}
+
 // Apply the epilogue to 32 consecutive accumulator columns of one row and
 // store them. `full` = all 32 columns are inside N and the stores may be
 // vectorized.
-template <int EPI>
+template <int EPI, bool I8>
 __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int row, int n, bool full,
                                                  const uint32_t (&acc)[32]) {
   float v[32];
+  if constexpr (I8) {
+    dequant32(a, a.sa[row], n, acc, v);
+  } else {
 #pragma unroll
-  for (int j = 0; j < 32; j++) v[j] = __uint_as_float(acc[j]);
+    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(acc[j]);
+  }
   if (a.bias) {
     if (full) {
 #pragma unroll
@@ -90,6 +135,7 @@ __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int row, int
     for (int j = 0; j < 16; j++)
       w[j] = gelu_poly4_bf16x2_rne(pack_bf16x2_rne(v[2 * j], v[2 * j + 1]));
     if constexpr (EPI == WX_EPI_BF16_GELU) {
+      if (a.rowmax) rowmax_update(a.rowmax, row, absmax_bf16x2(w, a.N - n));
       uint16_t* c = reinterpret_cast<uint16_t*>(a.C) + (int64_t)row * a.ldc + n;
       if (full) {
 #pragma unroll
@@ -140,21 +186,19 @@ __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int row, int
         if (n + j < a.N) c[j] = v[j];
     }
   } else {
+    uint32_t w[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) w[j] = pack_bf16x2_rne(v[2 * j], v[2 * j + 1]);
+    if (a.rowmax) rowmax_update(a.rowmax, row, absmax_bf16x2(w, a.N - n));
     uint16_t* c = reinterpret_cast<uint16_t*>(a.C) + (int64_t)row * a.ldc + n;
     if (full) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 o;
-        o.x = pack_bf16x2_rne(v[j], v[j + 1]);
-        o.y = pack_bf16x2_rne(v[j + 2], v[j + 3]);
-        o.z = pack_bf16x2_rne(v[j + 4], v[j + 5]);
-        o.w = pack_bf16x2_rne(v[j + 6], v[j + 7]);
-        *reinterpret_cast<uint4*>(c + j) = o;
-      }
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<uint4*>(c + 2 * j) = make_uint4(w[j], w[j + 1], w[j + 2], w[j + 3]);
     } else {
 #pragma unroll
       for (int j = 0; j < 32; j++)
-        if (n + j < a.N) c[j] = (uint16_t)bf16_bits<RND_RNE>(v[j]);
+        if (n + j < a.N) c[j] = (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
     }
   }
 }
@@ -196,18 +240,24 @@ __device__ __forceinline__ void add_bias32(const GemmArgs& a, int n, float (&v)[
 // threads of each shared-memory phase hit eight different bank groups).
 // t_col: tensor-memory address of the chunk's first column for this warp's
 // lanes; n: its first output column. WX_EPI_F32_RESID finds the residual in
-// the buffer and adds it.
-template <int EPI>
-__device__ __forceinline__ void epi_chunk_to_smem(const GemmArgs& a, uint32_t t_col, int n,
-                                                  uint8_t* rowp, int lane) {
+// the buffer and adds it. s_row: the row's int8 scale (I8). Returns, for the
+// bf16 outputs, max |value| over the chunk's columns inside N as bf16
+// magnitude bits (0 otherwise).
+template <int EPI, bool I8>
+__device__ __forceinline__ uint32_t epi_chunk_to_smem(const GemmArgs& a, uint32_t t_col, int n,
+                                                      uint8_t* rowp, int lane, float s_row) {
   const int sw = lane & 7;
   if constexpr (TmaEpi<EPI>::kF32) {
     uint32_t r[32];
     tmem_ld32(t_col, r);
     tmem_wait_ld();
     float v[32];
+    if constexpr (I8) {
+      dequant32(a, s_row, n, r, v);
+    } else {
 #pragma unroll
-    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+      for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+    }
     add_bias32(a, n, v);
 #pragma unroll
     for (int j = 0; j < 8; j++) {
@@ -218,16 +268,22 @@ __device__ __forceinline__ void epi_chunk_to_smem(const GemmArgs& a, uint32_t t_
       }
       *p = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
+    return 0u;
   } else {
     uint32_t r0[32], r1[32];
     tmem_ld32(t_col, r0);
     tmem_ld32(t_col + 32, r1);
     tmem_wait_ld();
+    uint32_t mx = 0;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       float v[32];
+      if constexpr (I8) {
+        dequant32(a, s_row, n + 32 * h, h ? r1 : r0, v);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 32; j++) v[j] = __uint_as_float(h ? r1[j] : r0[j]);
+        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(h ? r1[j] : r0[j]);
+      }
       add_bias32(a, n + 32 * h, v);
       uint32_t w[16];
 #pragma unroll
@@ -243,18 +299,40 @@ __device__ __forceinline__ void epi_chunk_to_smem(const GemmArgs& a, uint32_t t_
       for (int q = 0; q < 4; q++)
         *reinterpret_cast<uint4*>(rowp + (((4 * h + q) ^ sw) << 4)) =
             make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      if (a.rowmax) mx = max(mx, absmax_bf16x2(w, a.N - n - 32 * h));
     }
+    return mx;
+  }
+}
+
+// One K step of the MMA issuer: 4 instructions of K = 32 bytes (16 bf16 or
+// 32 int8 elements); the descriptor address advances by 2 (16-byte units).
+template <bool I8>
+__device__ __forceinline__ void umma_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                           uint32_t hi, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (I8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "mov.b64 ad, {%1, %5};\n\t"
+        "mov.b64 bd, {%2, %5};\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], ad, bd, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(hi)
+        : "memory");
+  } else {
+    umma_bf16_ss_lo(d_tmem, a_lo, b_lo, hi, idesc, accumulate);
   }
 }
 
 constexpr int kGemmThreads = 320;
 constexpr int kGemmEpiThreads = 256;
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool I8>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
   using Cfg = GemmCfg<BN>;
+  constexpr int kKElems = I8 ? 2 * kGemmBK : kGemmBK;   // elements per 128-byte K step
   constexpr int S = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -308,8 +386,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           issued |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tma_load_2d(&tmA, &full[stage], sA + stage * Cfg::A_BYTES, kb * kGemmBK, m0);
-          tma_load_2d(&tmB, &full[stage], sB + stage * Cfg::B_BYTES, kb * kGemmBK, n0);
+          tma_load_2d(&tmA, &full[stage], sA + stage * Cfg::A_BYTES, kb * kKElems, m0);
+          tma_load_2d(&tmB, &full[stage], sB + stage * Cfg::B_BYTES, kb * kKElems, n0);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
@@ -322,7 +400,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr uint32_t idesc = idesc_bf16_f32(kGemmBM, BN, 0, 0);
+      constexpr uint32_t idesc = I8 ? idesc_s8_s32(kGemmBM, BN) : idesc_bf16_f32(kGemmBM, BN, 0, 0);
       const uint32_t hi = kSdescHiSw128;
       const uint32_t a_lo = sdesc_lo(smem_u32(sA), 16), b_lo = sdesc_lo(smem_u32(sB), 16);
       int stage = 0, acc = 0;
@@ -339,7 +417,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t bd = b_lo + (uint32_t)(stage * (Cfg::B_BYTES >> 4));
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; k++)   // 32 bytes of K per MMA: +2
-            umma_bf16_ss_lo(d_tmem, ad + 2 * k, bd + 2 * k, hi, idesc, (kb | k) != 0);
+            umma_ss_lo<I8>(d_tmem, ad + 2 * k, bd + 2 * k, hi, idesc, (kb | k) != 0);
           umma_commit(&empty[stage]);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
@@ -385,7 +463,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint32_t r[32];
         tmem_ld32(t_row + (uint32_t)(c * 32), r);
         tmem_wait_ld();
-        if (row < a.M) epilogue_store32<EPI>(a, row, n, n + 32 <= a.N, r);
+        if (row < a.M) epilogue_store32<EPI, I8>(a, row, n, n + 32 <= a.N, r);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -477,6 +555,22 @@ __device__ __forceinline__ void umma_bf16_ss_lo_pair(uint32_t d_tmem, uint32_t a
       "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(hi)
       : "memory");
 }
+template <bool I8>
+__device__ __forceinline__ void umma_ss_lo_pair(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                                uint32_t hi, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (I8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "mov.b64 ad, {%1, %5};\n\t"
+        "mov.b64 bd, {%2, %5};\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], ad, bd, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(hi)
+        : "memory");
+  } else {
+    umma_bf16_ss_lo_pair(d_tmem, a_lo, b_lo, hi, idesc, accumulate);
+  }
+}
 // Arrive on the mbarrier at shared::cluster address `bar` (either CTA of the
 // pair) once every cta_group::2 MMA issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
@@ -498,7 +592,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
                : "memory");
 }
 
-template <int EPI>
+template <int EPI, bool I8>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
@@ -506,6 +600,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
                       const __grid_constant__ CUtensorMap tmR, const GemmArgs a) {
   using Cfg = Gemm2Cfg<EPI>;
   constexpr int S = Cfg::STAGES;
+  constexpr int kKElems = I8 ? 2 * kGemmBK : kGemmBK;   // elements per 128-byte K step
   constexpr int BN = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -565,8 +660,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           if (!mbar_wait(&empty[stage], phase ^ 1, a.err)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kGemm2StageBytes);
           const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-          tma_load_2d_pair(&tmA, fb, sA + stage * kGemm2ABytes, kb * kGemmBK, m0 + (int)rank * 128);
-          tma_load_2d_pair(&tmB, fb, sB + stage * kGemm2BBytes, kb * kGemmBK, n0 + (int)rank * 128);
+          tma_load_2d_pair(&tmA, fb, sA + stage * kGemm2ABytes, kb * kKElems, m0 + (int)rank * 128);
+          tma_load_2d_pair(&tmB, fb, sB + stage * kGemm2BBytes, kb * kKElems, n0 + (int)rank * 128);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
@@ -574,7 +669,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (leader)
-      constexpr uint32_t idesc = idesc_bf16_f32(256, BN, 0, 0);
+      constexpr uint32_t idesc = I8 ? idesc_s8_s32(256, BN) : idesc_bf16_f32(256, BN, 0, 0);
       const uint32_t hi = kSdescHiSw128;
       const uint32_t a_lo = sdesc_lo(smem_u32(sA), 16), b_lo = sdesc_lo(smem_u32(sB), 16);
       int stage = 0, acc = 0;
@@ -590,7 +685,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           const uint32_t bd = b_lo + (uint32_t)(stage * (kGemm2BBytes >> 4));
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; k++)   // 32 bytes of K per MMA: +2
-            umma_bf16_ss_lo_pair(d_tmem, ad + 2 * k, bd + 2 * k, hi, idesc, (kb | k) != 0);
+            umma_ss_lo_pair<I8>(d_tmem, ad + 2 * k, bd + 2 * k, hi, idesc, (kb | k) != 0);
           umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
           umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -645,6 +740,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int r0 = (tile / nnb) * 256 + row_off, c0 = (tile % nnb) * BN + half * (BN / 2);
       const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16) +
                              (uint32_t)(acc * BN + half * (BN / 2));
+      const int row = r0 + lane;
+      float s_row = 0.0f;
+      if constexpr (I8) s_row = row < a.M ? a.sa[row] : 0.0f;
+      uint32_t mx = 0;
       for (int c = 0; c < nc; c++, k++) {
         uint8_t* buf = ebuf + (k & 1) * kEpiBufBytes;
         if constexpr (EPI == WX_EPI_F32_RESID) {
@@ -654,8 +753,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           if (lane == 0) bulk_wait_group_read<1>();   // the store of chunk k-2 has read buf
           __syncwarp();
         }
-        epi_chunk_to_smem<EPI>(a, t_row + (uint32_t)(c * kCols), c0 + c * kCols,
-                               buf + lane * 128, lane);
+        mx = max(mx, epi_chunk_to_smem<EPI, I8>(a, t_row + (uint32_t)(c * kCols), c0 + c * kCols,
+                                                 buf + lane * 128, lane, s_row));
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -668,6 +767,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         }
       }
       if (!ok) break;
+      if (!TmaEpi<EPI>::kF32 && a.rowmax && row < a.M) rowmax_update(a.rowmax, row, mx);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
@@ -708,7 +808,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         uint32_t r[32];
         tmem_ld32(t_row + (uint32_t)(c * 32), r);
         tmem_wait_ld();
-        if (row < a.M) epilogue_store32<EPI>(a, row, n, n + 32 <= a.N, r);
+        if (row < a.M) epilogue_store32<EPI, I8>(a, row, n, n + 32 <= a.N, r);
       }
       tc_fence_before();
       __syncwarp();
@@ -731,7 +831,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-static int gemm_prepare(int bn, int epi, bool pair);
+static int gemm_prepare(int bn, int epi, bool pair, bool i8);
 
 // CTA pairs (the 2-SM kernel) when the 256 x 256 tiles fill every SM pair at
 // least once; smaller problems spread better over single-SM tiles.
@@ -764,11 +864,10 @@ static int encode_epilogue_maps(GemmPlan* p, void* C, const float* R, int64_t M,
   return WX_OK;
 }
 
-// Build the tensor maps and launch arguments once; the encoder keeps plans for
-// its fixed buffers, the standalone entry point builds one per call.
-int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, const float* R,
-              void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
-              int64_t ldr, int epi, int force_bn) {
+static int gemm_plan_impl(GemmPlan* p, const void* A, const void* B, const float* bias,
+                          const float* R, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                          int64_t ldb, int64_t ldc, int64_t ldr, int epi, int force_bn, bool i8,
+                          const float* sa, const float* sw, float* rowmax) {
   if (M <= 0 || N <= 0 || K <= 0) return fail(WX_ERR_INVALID, "gemm: M, N, K must be > 0");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
     return fail(WX_ERR_UNSUPPORTED, "gemm: dimension exceeds 2^31");
@@ -778,13 +877,19 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
     return fail(WX_ERR_INVALID, "gemm: epilogue %d", epi);
   if (epi == WX_EPI_F32_RESID && !R) return fail(WX_ERR_INVALID, "gemm: residual is NULL");
   if (lda < K || ldb < K || ldc < N) return fail(WX_ERR_INVALID, "gemm: leading dimension too small");
-  if (lda % 8 || ldb % 8) return fail(WX_ERR_INVALID, "gemm: lda and ldb must be multiples of 8");
+  const int a_align = i8 ? 16 : 8;   // elements per 16 bytes
+  if (lda % a_align || ldb % a_align)
+    return fail(WX_ERR_INVALID, "gemm: lda and ldb must keep rows 16-byte aligned");
   const bool f32_out = epi == WX_EPI_F32 || epi == WX_EPI_F32_RESID || pos_epi;
   if (ldc % (f32_out ? 4 : 8)) return fail(WX_ERR_INVALID, "gemm: ldc must keep rows 16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(C) & 15) || (bias && (reinterpret_cast<uintptr_t>(bias) & 15)))
     return fail(WX_ERR_INVALID, "gemm: C and bias must be 16-byte aligned");
   if (R && ((reinterpret_cast<uintptr_t>(R) & 15) || ldr % 4 || ldr < N))
     return fail(WX_ERR_INVALID, "gemm: residual must be 16-byte aligned with ldr a multiple of 4");
+  if (i8 && (!sa || !sw || (reinterpret_cast<uintptr_t>(sw) & 15)))
+    return fail(WX_ERR_INVALID, "gemm: int8 needs row scales and 16-byte aligned column scales");
+  if (rowmax && f32_out)
+    return fail(WX_ERR_INVALID, "gemm: row maxima are collected for bf16 outputs only");
   const int nsm = sm_count();
   const int64_t mb = (M + kGemmBM - 1) / kGemmBM;
   int bn = force_bn;
@@ -793,19 +898,21 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
   const bool pair = force_bn == 0 && use_pair(M, N, nsm);
   int* err = device_error_word();
   if (!err) return fail(WX_ERR_CUDA, "gemm: device error word unavailable");
-  WX_TRY(encode_tensor_map_2d(&p->tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
-                              (uint64_t)M, (uint64_t)lda * 2, kGemmBK, kGemmBM,
-                              CU_TENSOR_MAP_SWIZZLE_128B));
-  WX_TRY(encode_tensor_map_2d(&p->tmB, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
-                              (uint64_t)N, (uint64_t)ldb * 2, kGemmBK, pair ? 128u : (uint32_t)bn,
-                              CU_TENSOR_MAP_SWIZZLE_128B));
+  // one K step is 128 bytes of every row: 64 bf16 or 128 int8 elements
+  const CUtensorMapDataType dt = i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int es = i8 ? 1 : 2;
+  const uint32_t kstep = (uint32_t)(128 / es);
+  WX_TRY(encode_tensor_map_2d(&p->tmA, A, dt, es, (uint64_t)K, (uint64_t)M, (uint64_t)lda * es,
+                              kstep, kGemmBM, CU_TENSOR_MAP_SWIZZLE_128B));
+  WX_TRY(encode_tensor_map_2d(&p->tmB, B, dt, es, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * es,
+                              kstep, pair ? 128u : (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B));
   GemmArgs& g = p->args;
   g.M = (int)M;
   g.N = (int)N;
   g.K = (int)K;
   g.num_n_blocks = (int)((N + bn - 1) / bn);
   g.num_tiles = (int)((pair ? (M + 255) / 256 : mb) * g.num_n_blocks);
-  g.num_k_blocks = (int)((K + kGemmBK - 1) / kGemmBK);
+  g.num_k_blocks = (int)((K + kstep - 1) / kstep);
   g.C = C;
   g.ldc = ldc;
   g.bias = bias;
@@ -815,12 +922,32 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
   g.pos = nullptr;
   g.ldp = 0;
   g.pos_T = 1;
+  g.sa = sa;
+  g.sw = sw;
+  g.rowmax = rowmax;
   p->bn = bn;
   p->epi = epi;
   p->pair = pair;
+  p->i8 = i8;
   p->grid = pair ? 2 * std::min(g.num_tiles, nsm / 2) : std::min(g.num_tiles, nsm);
   WX_TRY(encode_epilogue_maps(p, C, R, M, N, ldc, ldr, epi));
-  return gemm_prepare(bn, epi, pair);
+  return gemm_prepare(bn, epi, pair, i8);
+}
+
+// Build the tensor maps and launch arguments once; the encoder keeps plans for
+// its fixed buffers, the standalone entry point builds one per call.
+int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, const float* R,
+              void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+              int64_t ldr, int epi, int force_bn) {
+  return gemm_plan_impl(p, A, B, bias, R, C, M, N, K, lda, ldb, ldc, ldr, epi, force_bn, false,
+                        nullptr, nullptr, nullptr);
+}
+
+int gemm_plan_i8(GemmPlan* p, const void* A, const void* B, const float* sa, const float* sw,
+                 const float* bias, const float* R, void* C, int64_t M, int64_t N, int64_t K,
+                 int64_t lda, int64_t ldb, int64_t ldc, int64_t ldr, int epi, float* rowmax) {
+  return gemm_plan_impl(p, A, B, bias, R, C, M, N, K, lda, ldb, ldc, ldr, epi, 0, true, sa, sw,
+                        rowmax);
 }
 
 // The same plan without the library's device error word, whose first use on
@@ -868,57 +995,72 @@ int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, cons
   g.pos = nullptr;
   g.ldp = 0;
   g.pos_T = 1;
+  g.sa = nullptr;
+  g.sw = nullptr;
+  g.rowmax = nullptr;
   p->bn = bn;
   p->epi = epi;
   p->pair = pair;
+  p->i8 = false;
   p->grid = pair ? 2 * std::min(g.num_tiles, nsm / 2) : std::min(g.num_tiles, nsm);
   WX_TRY(encode_epilogue_maps(p, C, nullptr, M, N, ldc, 0, epi));
-  return gemm_prepare(bn, epi, pair);
+  return gemm_prepare(bn, epi, pair, false);
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool I8>
 static int set_attr_t() {
   static bool done[64] = {false};
   int dev = 0;
   WX_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 64 && done[dev]) return WX_OK;
-  WX_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_kernel<BN, EPI>,
+  WX_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_kernel<BN, EPI, I8>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM));
   if (dev < 64) done[dev] = true;
   return WX_OK;
 }
 
-template <int EPI>
+template <int EPI, bool I8>
 static int set_attr_pair_t() {
   static bool done[64] = {false};
   int dev = 0;
   WX_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 64 && done[dev]) return WX_OK;
-  WX_CUDA_TRY(cudaFuncSetAttribute(gemm2_bf16_kernel<EPI>,
+  WX_CUDA_TRY(cudaFuncSetAttribute(gemm2_bf16_kernel<EPI, I8>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    Gemm2Cfg<EPI>::SMEM));
   if (dev < 64) done[dev] = true;
   return WX_OK;
 }
 
-template <int BN, int EPI>
+template <int EPI, bool I8>
+static int prepare_t(int bn, bool pair) {
+  return pair ? set_attr_pair_t<EPI, I8>() : bn == 256 ? set_attr_t<256, EPI, I8>()
+                                                       : set_attr_t<128, EPI, I8>();
+}
+
+template <int BN, int EPI, bool I8>
 static int launch_t(const GemmPlan& p, cudaStream_t st) {
   if (p.pair) {
-    gemm2_bf16_kernel<EPI><<<p.grid, kGemmThreads, Gemm2Cfg<EPI>::SMEM, st>>>(p.tmA, p.tmB, p.tmC,
-                                                                              p.tmR, p.args);
-    return check_launch("gemm_bf16_pair");
+    gemm2_bf16_kernel<EPI, I8><<<p.grid, kGemmThreads, Gemm2Cfg<EPI>::SMEM, st>>>(
+        p.tmA, p.tmB, p.tmC, p.tmR, p.args);
+    return check_launch(I8 ? "gemm_i8_pair" : "gemm_bf16_pair");
   }
-  gemm_bf16_kernel<BN, EPI><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, st>>>(p.tmA, p.tmB,
-                                                                             p.args);
-  return check_launch("gemm_bf16");
+  gemm_bf16_kernel<BN, EPI, I8><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, st>>>(p.tmA, p.tmB,
+                                                                                 p.args);
+  return check_launch(I8 ? "gemm_i8" : "gemm_bf16");
+}
+
+template <int EPI, bool I8>
+static int run_t(const GemmPlan& p, cudaStream_t st) {
+  return p.bn == 256 ? launch_t<256, EPI, I8>(p, st) : launch_t<128, EPI, I8>(p, st);
 }
 
 // Kernel attributes are set when a plan is made, so that a captured launch
 // sequence contains nothing but launches.
-static int gemm_prepare(int bn, int epi, bool pair) {
+static int gemm_prepare(int bn, int epi, bool pair, bool i8) {
 #define WX_GEMM_PREP(E) \
   case E:               \
-    return pair ? set_attr_pair_t<E>() : bn == 256 ? set_attr_t<256, E>() : set_attr_t<128, E>();
+    return i8 ? prepare_t<E, true>(bn, pair) : prepare_t<E, false>(bn, pair);
   switch (epi) {
     WX_GEMM_PREP(WX_EPI_F32)
     WX_GEMM_PREP(WX_EPI_BF16)
@@ -934,9 +1076,9 @@ static int gemm_prepare(int bn, int epi, bool pair) {
 }
 
 int gemm_run(const GemmPlan& p, cudaStream_t st) {
-#define WX_GEMM_CASE(E)                                               \
-  case E:                                                             \
-    return p.bn == 256 ? launch_t<256, E>(p, st) : launch_t<128, E>(p, st);
+#define WX_GEMM_CASE(E) \
+  case E:               \
+    return p.i8 ? run_t<E, true>(p, st) : run_t<E, false>(p, st);
   switch (p.epi) {
     WX_GEMM_CASE(WX_EPI_F32)
     WX_GEMM_CASE(WX_EPI_BF16)

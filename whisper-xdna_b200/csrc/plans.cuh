@@ -17,6 +17,10 @@ struct GemmArgs {
   const float* pos;  // positional embedding (WX_EPI_*_POS), row (row % pos_T)
   int64_t ldp;
   int pos_T;
+  // int8 GEMM: C = epilogue((float(A_q @ B_q^T) * sa[row]) * sw[col])
+  const float* sa;   // per-row (token) scales of A
+  const float* sw;   // per-column (channel) scales of B
+  float* rowmax;     // bf16 outputs: max |value| of each row, atomically (or NULL)
 };
 
 // Epilogues used only inside the library (the conv2 step of the encoder):
@@ -32,12 +36,19 @@ struct GemmPlan {
   int grid;
   int epi;
   bool pair;   // 2-SM kernel (CTA pairs, 256 x 256 tiles)
+  bool i8;     // int8 operands (tcgen05 kind::i8), dequantised in the epilogue
 };
 
 // force_bn: 0 = pick, else 128 or 256 (output columns per tile)
 int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, const float* R,
               void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
               int64_t ldr, int epi, int force_bn);
+// The int8 GEMM: A (M x K) and B (N x K) int8, row-major; sa (M) and sw (N) the
+// dequantisation scales; rowmax (M floats, or NULL) collects max |C| per row
+// for the bf16 epilogues.
+int gemm_plan_i8(GemmPlan* p, const void* A, const void* B, const float* sa, const float* sw,
+                 const float* bias, const float* R, void* C, int64_t M, int64_t N, int64_t K,
+                 int64_t lda, int64_t ldb, int64_t ldc, int64_t ldr, int epi, float* rowmax);
 int gemm_run(const GemmPlan& p, cudaStream_t st);
 int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, const float* bias,
                                  void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
@@ -73,5 +84,12 @@ int launch_softmax_rows(const void* in, void* out, int64_t rows, int64_t cols, i
 int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, const float* beta,
                           void* out, int out_dtype, int64_t rows, int64_t cols, int64_t ld_in,
                           int64_t ld_out, float eps, int mode, int rounding, cudaStream_t st);
+
+// int8 quantisation (quant.cu)
+int launch_absmax_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld,
+                       float* out, int64_t out_stride, cudaStream_t st);
+int launch_quantize_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld,
+                         const float* rowmax, int64_t rowmax_stride, int8_t* q, int64_t ld_q,
+                         float* scale, cudaStream_t st);
 
 }  // namespace wx

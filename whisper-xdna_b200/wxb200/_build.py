@@ -19,7 +19,7 @@ ROOT = PKG.parents[1]
 BUILD = ROOT / "_build"
 LIB = PKG / "libwxb200.so"
 SOURCES = ["capi.cu", "rowops.cu", "gemm.cu", "attention.cu", "encoder.cu", "noalloc.cu",
-           "mel.cu"]
+           "mel.cu", "quant.cu"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3",
               "-std=c++17", "-Xcompiler", "-fPIC"]
 

@@ -29,6 +29,9 @@ WX_EPI_BF16_GELU = 3
 WX_EPI_BF16_GELU_ERF = 4
 WX_GELU_POLY4 = 0
 WX_GELU_ERF = 1
+WX_QUANT_NONE = 0
+WX_QUANT_INT8_PERCHAN = 1
+WX_QUANT_INT8_PERTENSOR = 2
 
 _c = ctypes
 _p, _i, _i64, _f = _c.c_void_p, _c.c_int, _c.c_int64, _c.c_float
@@ -44,6 +47,10 @@ SIGNATURES = {
     "wx_softmax_exp_table": (_i, [_i, _p, _p, _i64]),
     "wx_gelu4_table": (_i, [_i, _p, _i64]),
     "wx_gemm_bf16": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p]),
+    "wx_absmax_rows": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p]),
+    "wx_quantize_rows": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _p]),
+    "wx_gemm_i8": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i,
+                        _p, _p]),
     "wx_attention": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p]),
     "wx_mlp_bf16_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),
     "wx_encoder_create": (_i, [_c.POINTER(_p), _i, _i, _i, _i, _i, _i, _i, _i]),
@@ -51,6 +58,7 @@ SIGNATURES = {
     "wx_encoder_set_frontend": (_i, [_p, _p, _p, _p, _p, _p]),
     "wx_encoder_set_layer": (_i, [_p, _i] + [_p] * 15),
     "wx_encoder_set_ln_post": (_i, [_p, _p, _p]),
+    "wx_encoder_set_quant": (_i, [_p, _i]),
     "wx_encoder_forward": (_i, [_p, _p, _p, _i64, _i64, _i, _p]),
     "wx_encoder_forward_host": (_i, [_p, _p, _p, _i64, _i64, _i, _p]),
     "wx_encoder_device_bytes": (_i64, [_p]),

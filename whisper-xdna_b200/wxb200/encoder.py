@@ -45,9 +45,18 @@ class Encoder:
     gelu: "poly4" -- the reference's device GELU (g4f / g4r: the RNE piecewise
     polynomial of kernels/gelu_poly4_eval.inc), "erf" -- exact erf-GELU (the
     reference's numpy path).
+    quant: None (bf16 GEMMs), "int8-perchan" or "int8-pertensor" -- the
+    reference's int8 projection/MLP mode (bench/probe_int8_decode.py:48-74):
+    int8 operands on the int8 tensor cores, per-token activation scales,
+    per-channel or per-matrix weight scales. The probe runs it with the erf
+    GELU, so pass gelu="erf" to follow it.
     """
 
-    def __init__(self, W, n_layer=None, n_head=None, max_batch=1, gelu="poly4", device=None):
+    QUANT_MODES = {None: L.WX_QUANT_NONE, "int8-perchan": L.WX_QUANT_INT8_PERCHAN,
+                   "int8-pertensor": L.WX_QUANT_INT8_PERTENSOR}
+
+    def __init__(self, W, n_layer=None, n_head=None, max_batch=1, gelu="poly4", device=None,
+                 quant=None):
         if not torch.cuda.is_available():
             raise RuntimeError("the B200 encoder needs a CUDA device; there is no CPU fallback")
         self.device = torch.device("cuda", torch.cuda.current_device() if device is None
@@ -57,12 +66,18 @@ class Encoder:
         self.max_batch = int(max_batch)
         self.gelu = gelu
         mode = {"poly4": L.WX_GELU_POLY4, "erf": L.WX_GELU_ERF}[gelu]
+        if quant not in self.QUANT_MODES:
+            raise ValueError(f"quant must be one of {list(self.QUANT_MODES)}")
+        self.quant = quant
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             L.check(L.lib().wx_encoder_create(ctypes.byref(h), self.n_mels, self.d,
                                               self.n_head, self.n_layer, self.ffn,
                                               self.n_ctx, self.max_batch, mode))
         self._h = h
+        if quant is not None:
+            with torch.cuda.device(self.device):
+                L.check(L.lib().wx_encoder_set_quant(h, self.QUANT_MODES[quant]))
         self._load(W)
 
     def _load(self, W):

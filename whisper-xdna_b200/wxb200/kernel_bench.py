@@ -3,6 +3,8 @@
     PYTHONPATH=whisper-xdna_b200 python -m wxb200.kernel_bench --kernel attention --batch 4
 
 Kernels: attention, fc1 (GEMM + GELU), fc2 (GEMM + residual), qkv, outproj,
+their int8 twins fc1_i8, fc2_i8, qkv_i8, outproj_i8 (the int8 mode's GEMMs),
+quantize_bf16 (fc2's input rows, maxima given) and quantize_f32 (an LN output),
 layernorm (fp32 -> bf16, the encoder's), and the standalone row ops at the
 BASELINE row-op sizes: gelu (g4r 1500x5120), gelu_f32 (g4f 1500x5120), softmax
 (s4r 20x1500x1500, scale 1/8), layernorm_gb (1500x1280 with gamma/beta), and
@@ -49,6 +51,39 @@ def setup(kernel, batch, dev="cuda"):
             fn = lambda: ops.gemm(A, W, bias=b, out=C, epilogue=epi)
             byt = M * K * 2 + N * K * 2 + M * N * 2
         return fn, 2.0 * M * N * K, byt
+    if kernel in ("fc1_i8", "fc2_i8", "qkv_i8", "outproj_i8"):
+        # the int8 mode's GEMMs (int8 operands, s32 accumulation, dequantising epilogue)
+        base = kernel[:-3]
+        K, N = {"fc1": (D, FFN), "fc2": (FFN, D), "qkv": (D, 3 * D), "outproj": (D, D)}[base]
+        Aq = torch.randint(-127, 128, (M, K), device=dev, dtype=torch.int8, generator=g)
+        Wq = torch.randint(-127, 128, (N, K), device=dev, dtype=torch.int8, generator=g)
+        sa = torch.rand(M, device=dev, generator=g) * 1e-2
+        sw = torch.rand(N, device=dev, generator=g) * 1e-3
+        b = torch.zeros(N, device=dev)
+        if base in ("fc2", "outproj"):
+            x = rn(M, N)
+            fn = lambda: ops.gemm_i8(Aq, Wq, sa, sw, bias=b, residual=x, out=x,
+                                     epilogue=L.WX_EPI_F32_RESID)
+            byt = M * K + N * K + 2 * M * N * 4
+        else:
+            C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            epi = L.WX_EPI_BF16_GELU if base == "fc1" else L.WX_EPI_BF16
+            rm = torch.zeros(M, device=dev) if base == "fc1" else None
+            fn = lambda: ops.gemm_i8(Aq, Wq, sa, sw, bias=b, out=C, epilogue=epi, rowmax=rm)
+            byt = M * K + N * K + M * N * 2
+        return fn, 2.0 * M * N * K, byt
+    if kernel in ("quantize_bf16", "quantize_f32"):
+        # per-token quantisation of the fc2 input (bf16, M x ffn, maxima given)
+        # or of an LN output (fp32, M x d)
+        if kernel == "quantize_bf16":
+            x = rn(M, FFN).to(torch.bfloat16)
+            rm = x.float().abs().amax(dim=1)
+        else:
+            x, rm = rn(M, D), None
+        q = torch.empty(x.shape, device=dev, dtype=torch.int8)
+        sc = torch.empty(M, device=dev)
+        fn = lambda: ops.quantize_rows(x, rowmax=rm, q=q, scale=sc)
+        return fn, 0.0, x.numel() * (x.element_size() + 1) + M * 4
     if kernel == "layernorm":
         x = rn(M, D)
         h = torch.empty(M, D, device=dev, dtype=torch.bfloat16)

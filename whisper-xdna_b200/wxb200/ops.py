@@ -117,6 +117,92 @@ def gemm(A, W, bias=None, residual=None, out=None, epilogue=None):
     return out
 
 
+def _outvec(t, n, name):
+    """A float32 CUDA vector written in place: must be contiguous already."""
+    _vec(t, n, name)
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def _dtype_code(t, name):
+    if t.dtype == torch.bfloat16:
+        return L.WX_DTYPE_BF16
+    if t.dtype == torch.float32:
+        return L.WX_DTYPE_F32
+    raise TypeError(f"{name}: bf16 or fp32 expected, got {t.dtype}")
+
+
+def absmax_rows(x, out=None, per_row=True):
+    """max |x| per row (per_row) or over the whole matrix, folded into `out`
+    (fp32, zeroed when created here)."""
+    _mat(x, "x", (torch.bfloat16, torch.float32))
+    rows, cols = x.shape
+    if out is None:
+        out = torch.zeros(rows if per_row else 1, dtype=torch.float32, device=x.device)
+    _outvec(out, rows if per_row else 1, "out")
+    L.check(L.lib().wx_absmax_rows(_ptr(x), _dtype_code(x, "x"), rows, cols, x.stride(0),
+                                   _ptr(out), 1 if per_row else 0, _stream()))
+    return out
+
+
+def quantize_rows(x, rowmax=None, q=None, scale=None):
+    """Per-row int8 quantisation: scale = max|row| / 127 (1 for a zero row),
+    q = rint(x / scale). rowmax: precomputed maxima, one per row or a single
+    value for every row. Returns (q int8 (rows, cols), scale fp32 (rows,))."""
+    _mat(x, "x", (torch.bfloat16, torch.float32))
+    rows, cols = x.shape
+    if q is None:
+        q = torch.empty(rows, (cols + 15) // 16 * 16, dtype=torch.int8, device=x.device)[:, :cols]
+    _mat(q, "q", (torch.int8,))
+    if scale is None:
+        scale = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _outvec(scale, rows, "scale")
+    stride = 0
+    if rowmax is not None:
+        if rowmax.numel() not in (1, rows):
+            raise ValueError("rowmax: one value per row or one in all")
+        stride = 1 if rowmax.numel() == rows and rows > 1 else 0
+        rowmax = _vec(rowmax, rowmax.numel(), "rowmax")
+    L.check(L.lib().wx_quantize_rows(_ptr(x), _dtype_code(x, "x"), rows, cols, x.stride(0),
+                                     _ptr(rowmax), stride, _ptr(q), q.stride(0), _ptr(scale),
+                                     _stream()))
+    return q, scale
+
+
+def gemm_i8(Aq, Wq, sa, sw, bias=None, residual=None, out=None, epilogue=None, rowmax=None):
+    """epilogue((float(Aq @ Wq^T) * sa[:, None]) * sw[None, :]) on the int8
+    tensor cores: Aq (M, K) and Wq (N, K) int8 with rows 16-byte aligned, sa
+    (M,) and sw (N,) fp32. rowmax (M,) fp32 collects max |out| per row for the
+    bf16 epilogues."""
+    _mat(Aq, "Aq", (torch.int8,))
+    _mat(Wq, "Wq", (torch.int8,))
+    M, K = Aq.shape
+    N, K2 = Wq.shape
+    if K != K2:
+        raise ValueError(f"inner dimensions differ: {K} vs {K2}")
+    if epilogue is None:
+        epilogue = L.WX_EPI_F32_RESID if residual is not None else L.WX_EPI_F32
+    f32_out = epilogue in (L.WX_EPI_F32, L.WX_EPI_F32_RESID)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32 if f32_out else torch.bfloat16,
+                          device=Aq.device)
+    _mat(out, "out", (torch.float32,) if f32_out else (torch.bfloat16,))
+    sa = _vec(sa, M, "sa")
+    sw = _vec(sw, N, "sw")
+    b = _vec(bias, N, "bias")
+    if rowmax is not None:
+        _outvec(rowmax, M, "rowmax")
+    r = None
+    if residual is not None:
+        r = _mat(residual, "residual", (torch.float32,))
+    L.check(L.lib().wx_gemm_i8(_ptr(Aq), _ptr(Wq), _ptr(sa), _ptr(sw), _ptr(b), _ptr(r),
+                               _ptr(out), M, N, K, Aq.stride(0), Wq.stride(0), out.stride(0),
+                               r.stride(0) if r is not None else 0, epilogue, _ptr(rowmax),
+                               _stream()))
+    return out
+
+
 def attention(q, k, v, n_batch, n_head, scale, out=None):
     """softmax(scale * q k^T) v per (batch, head); q, k, v: (n_batch*T, n_head*64)
     bf16 (column slices of one QKV buffer are fine)."""
