@@ -50,19 +50,28 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-layers", type=int, default=2,
                     help="layers in the bounded CPU sample")
+    ap.add_argument("--quant", choices=["none", "int8-perchan", "int8-pertensor"],
+                    default="none",
+                    help="int8 projection/MLP mode (the reference's int8 probe); not the "
+                         "headline configuration, which is bf16")
     return ap.parse_args()
 
 
-def arm_config(batch, world):
+def arm_config(batch, world, quant="none"):
     """The workload both arms report (the reference arm times a bounded sample
     of it)."""
-    return {"workload": f"large-v3 encoder forward, ctx 1500, {batch} clips per GPU per step "
-                        "(BASELINE batch-64 config, clip-sharded)",
-            "model": "whisper large-v3 encoder (32 layers, d 1280, 20x64 heads, ffn 5120)",
-            "global_batch": batch * world, "seq_len": CTX,
-            "parallelism": f"dp{world} (independent replicas, no collective)",
-            "gelu": "poly4 RNE (the reference's device GELU)",
-            "l2": "inputs larger than L2 (no flush)", "cuda_graph": True}
+    cfg = {"workload": f"large-v3 encoder forward, ctx 1500, {batch} clips per GPU per step "
+                       "(BASELINE batch-64 config, clip-sharded)",
+           "model": "whisper large-v3 encoder (32 layers, d 1280, 20x64 heads, ffn 5120)",
+           "global_batch": batch * world, "seq_len": CTX,
+           "parallelism": f"dp{world} (independent replicas, no collective)",
+           "gelu": "poly4 RNE (the reference's device GELU)",
+           "l2": "inputs larger than L2 (no flush)", "cuda_graph": True}
+    if quant != "none":
+        cfg["quant"] = (f"{quant}: int8 conv/QKV/out-proj/fc1/fc2 GEMMs with per-token "
+                        "activation scales (bench/probe_int8_decode.py:48-74), bf16 attention")
+        cfg["gelu"] = "exact erf (the int8 probe's host GELU)"
+    return cfg
 
 
 # ------------------------------------------------------------------ CPU side
@@ -256,7 +265,8 @@ def run_b200(args, rank, world, local_rank):
 
     B = args.batch
     W = make_weights_fast(seed=1)
-    enc = Encoder(W, max_batch=B, gelu="poly4")
+    quant = None if args.quant == "none" else args.quant
+    enc = Encoder(W, max_batch=B, gelu="poly4" if quant is None else "erf", quant=quant)
     del W
     # per-clip seeded mel, pinned host copy for the end-to-end leg
     g = torch.Generator().manual_seed(1000 + rank)
@@ -324,7 +334,7 @@ def run_b200(args, rank, world, local_rank):
                 "whole_step": {"achieved": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12,
                                "frac": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12
                                / peaks["bf16_tflops"]}}
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and quant is None:
             v, spent, desc = cpu_sample(args.cpu_layers)
             cpu = {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
                    "sample": desc + f"; {spent:.1f} s of CPU time"}
@@ -335,13 +345,18 @@ def run_b200(args, rank, world, local_rank):
             "ms_per_step": t_dev / args.steps * 1e3,
             "ms_per_clip_per_gpu": t_dev / args.steps * 1e3 / B,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (random N(0,0.02) large-v3 weights, "
-                                     "U[-0.8,1.2] log-mel per clip)",
-            "config": arm_config(B, world),
+            "dtype": "bf16" if quant is None else "int8 GEMMs (s32 accumulation), bf16 attention",
+            "data": "synthetic (random N(0,0.02) large-v3 weights, U[-0.8,1.2] log-mel per clip)",
+            "config": arm_config(B, world, args.quant),
             "e2e": {"value": e2e, "unit": UNIT,
                     "h2d_bytes_per_step": int(mel_host.numel() * 4),
                     "d2h_bytes_per_step": int(out_host.numel() * 4)},
-            "gpu_launches": (2 + 2 + 7 * N_LAYER + 1) * args.steps,
+            # per step: im2col, [quantise,] GEMM for each conv; per layer LN, QKV,
+            # attention, out-proj, LN, fc1, fc2 (+ the quantisation of O and of
+            # fc1's output in int8 mode, where LN and quantisation are one kernel);
+            # ln_post
+            "gpu_launches": ((2 + 2 + 7 * N_LAYER + 1) if quant is None
+                             else (3 + 3 + 9 * N_LAYER + 1)) * args.steps,
             "roofline": roof, "kernels": kernels, "row_ops": row_ops, "clocks": clk,
             "cpu_baseline": cpu, "output_finite": finite,
             "flop_per_clip": FLOP_PER_CLIP,

@@ -156,6 +156,13 @@ int wx_gemm_bf16(const void* A, const void* B, const float* bias, const float* R
  * stored bf16 values by an atomic fold, for quantising C as the next GEMM's A. */
 int wx_absmax_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld_in,
                    float* out, int64_t out_stride, void* stream);
+/* The encoder's fp32 LayerNorm (wx_layernorm_rows, WX_LN_FP32, fp32 in) fused
+ * with wx_quantize_rows of its output: q and scale equal those two calls in
+ * sequence. cols <= 2048 and a multiple of 4; in, gamma, beta 16-byte aligned
+ * (gamma/beta may be NULL), q 4-byte aligned with ld_q a multiple of 4. */
+int wx_layernorm_quant_rows(const float* in, const float* gamma, const float* beta, int8_t* q,
+                            float* scale, int64_t rows, int64_t cols, int64_t ld_in, int64_t ld_q,
+                            float eps, void* stream);
 int wx_quantize_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld_in,
                      const float* rowmax, int64_t rowmax_stride, int8_t* q, int64_t ld_q,
                      float* scale, void* stream);

@@ -57,6 +57,44 @@ def test_quantize_rows_matches_numpy(cuda, dtype, rows, cols):
     assert np.array_equal(q.cpu().numpy(), rq)
 
 
+def test_quantize_rows_at_rounding_ties(cuda):
+    """Values at and one or two ulps around (k + 1/2) * scale, over scales
+    from 1e-6 to 1e6: the quotient's rounding decides the integer, so this is
+    where a division that is not correctly rounded would show."""
+    rng = np.random.default_rng(11)
+    rows = []
+    for _ in range(64):
+        s0 = np.float32(10.0 ** rng.uniform(-6, 6))
+        sa = np.float32(np.float32(127) * s0) / np.float32(127)   # the kernel's scale
+        k = rng.integers(-127, 127, 400).astype(np.float32)
+        t = ((k + np.float32(0.5)) * sa).astype(np.float32)
+        vals = [t, np.nextafter(t, np.float32(np.inf)), np.nextafter(t, np.float32(-np.inf)),
+                np.nextafter(np.nextafter(t, np.float32(np.inf)), np.float32(np.inf))]
+        # the maximum, the tie region, and zeros to a multiple of 4 columns
+        # (the 16-byte vector path)
+        row = np.concatenate([[np.float32(127) * s0]] + vals + [np.zeros(3)]).astype(np.float32)
+        row = np.clip(row, -np.float32(127) * s0, np.float32(127) * s0)
+        rows.append(row)
+    x = np.stack(rows)
+    q, s = ops.quantize_rows(torch.from_numpy(x).cuda())
+    rq, rs = Q.quantize_rows(x)
+    assert np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(q.cpu().numpy(), rq)
+
+
+@pytest.mark.parametrize("rows,cols", [(300, 1280), (77, 384), (9, 2048), (5, 100)])
+def test_layernorm_quant_equals_two_passes(cuda, rows, cols):
+    g = torch.Generator().manual_seed(cols)
+    x = (torch.randn(rows, cols, generator=g) * 3 + 1).cuda()
+    gm = (torch.rand(cols, generator=g) + 0.5).cuda()
+    bt = (torch.randn(cols, generator=g) * 0.1).cuda()
+    x[rows // 2] = 2.0                                  # constant row: LN output = beta
+    q, s = ops.layer_norm_quant_rows(x, gm, bt)
+    h = ops.layer_norm_rows(x, gm, bt, out=torch.empty_like(x), mode=L.WX_LN_FP32)
+    q2, s2 = ops.quantize_rows(h)
+    assert torch.equal(s, s2) and torch.equal(q, q2)
+
+
 def test_quantize_rows_given_maxima(cuda):
     x = torch.randn(40, 96, generator=torch.Generator().manual_seed(3)).cuda()
     m = ops.absmax_rows(x)

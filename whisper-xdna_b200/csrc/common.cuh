@@ -436,6 +436,39 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn_maj
          ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------- int8 quantisation
+// x / s rounded to nearest (IEEE), for a per-row divisor s with rcp = RN(1/s)
+// (__frcp_rn): q = RN(x * rcp) is within one ulp of x / s, the residual
+// x - s*q is exact in one FMA, and RN(q + residual * rcp) is then the correctly
+// rounded quotient (Markstein's theorem; P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990). It holds while nothing overflows or goes subnormal, so
+// callers use it for s in [2^-100, 2^100] and |x| < 2^100 only.
+__device__ __forceinline__ float2 div2_rn(float2 x, float2 s, float2 rcp) {
+  const float2 q = __fmul2_rn(x, rcp);
+  const float2 r = __ffma2_rn(make_float2(-q.x, -q.y), s, x);
+  return __ffma2_rn(r, rcp, q);
+}
+__device__ __forceinline__ bool div2_rn_safe(float s) {
+  return s >= 7.8886091e-31f && s <= 1.2676506e30f;   // 2^-100 .. 2^100
+}
+// rint(x / s) of four values as packed int8 (half to even; |x / s| <= 127.5)
+__device__ __forceinline__ uint32_t quant4_i8(float x0, float x1, float x2, float x3, float s,
+                                              float rcp, bool fast) {
+  float q0, q1, q2, q3;
+  if (fast) {
+    const float2 s2 = make_float2(s, s), r2 = make_float2(rcp, rcp);
+    const float2 a = div2_rn(make_float2(x0, x1), s2, r2);
+    const float2 b = div2_rn(make_float2(x2, x3), s2, r2);
+    q0 = a.x; q1 = a.y; q2 = b.x; q3 = b.y;
+  } else {
+    q0 = __fdiv_rn(x0, s); q1 = __fdiv_rn(x1, s); q2 = __fdiv_rn(x2, s); q3 = __fdiv_rn(x3, s);
+  }
+  return ((uint32_t)__float2int_rn(q0) & 0xFFu) | (((uint32_t)__float2int_rn(q1) & 0xFFu) << 8) |
+         (((uint32_t)__float2int_rn(q2) & 0xFFu) << 16) |
+         (((uint32_t)__float2int_rn(q3) & 0xFFu) << 24);
+}
+
 // Instruction descriptor, kind::i8: s32 accumulator (bits 4-5 = 2), signed
 // 8-bit A and B (bits 7-9, 10-12 = 1), both K-major, N >> 3, M >> 4.
 __host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {

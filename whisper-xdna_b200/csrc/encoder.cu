@@ -341,6 +341,18 @@ static int build_plans(wx_encoder* e, int64_t B, int64_t T, Plans** out) {
   return WX_OK;
 }
 
+// LayerNorm of the residual stream quantised per token into aq / sa: one
+// fused kernel up to width 2048, else LN to fp32 (in h32) and a quantise pass.
+static int ln_quant(wx_encoder* e, const float* x, const float* g, const float* b, float* h32,
+                    int64_t M, cudaStream_t st) {
+  const int64_t d = e->d;
+  if (d <= 2048)
+    return launch_layernorm_quant_rows(x, g, b, e->aq, e->sa, M, d, d, d, 1e-5f, st);
+  WX_TRY(launch_layernorm_rows(x, WX_DTYPE_F32, g, b, h32, WX_DTYPE_F32, M, d, d, d, 1e-5f,
+                               WX_LN_FP32, WX_ROUND_RNE, st));
+  return launch_quantize_rows(h32, WX_DTYPE_F32, M, d, d, nullptr, 0, e->aq, d, e->sa, st);
+}
+
 // The launch sequence of one int8-mode forward pass.
 static int forward_launches_i8(wx_encoder* e, Plans* p, const float* mel, float* out, int64_t B,
                                int64_t T, cudaStream_t st) {
@@ -365,16 +377,12 @@ static int forward_launches_i8(wx_encoder* e, Plans* p, const float* mel, float*
   WX_TRY(gemm_run(p->conv2, st));
   for (int l = 0; l < e->nl; l++) {
     const LayerW& w = e->L[l];
-    WX_TRY(launch_layernorm_rows(e->x, WX_DTYPE_F32, w.ln1_g, w.ln1_b, h32, WX_DTYPE_F32, M, d, d,
-                                 d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st));
-    WX_TRY(launch_quantize_rows(h32, WX_DTYPE_F32, M, d, d, nullptr, 0, e->aq, d, e->sa, st));
+    WX_TRY(ln_quant(e, e->x, w.ln1_g, w.ln1_b, h32, M, st));
     WX_TRY(gemm_run(p->qkv[l], st));
     WX_TRY(attn_run(p->attn, st));
     WX_TRY(launch_quantize_rows(e->o, WX_DTYPE_BF16, M, d, d, nullptr, 0, e->aq, d, e->sa, st));
     WX_TRY(gemm_run(p->out[l], st));
-    WX_TRY(launch_layernorm_rows(e->x, WX_DTYPE_F32, w.ln2_g, w.ln2_b, h32, WX_DTYPE_F32, M, d, d,
-                                 d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st));
-    WX_TRY(launch_quantize_rows(h32, WX_DTYPE_F32, M, d, d, nullptr, 0, e->aq, d, e->sa, st));
+    WX_TRY(ln_quant(e, e->x, w.ln2_g, w.ln2_b, h32, M, st));
     WX_CUDA_TRY(cudaMemsetAsync(e->rowmax, 0, (size_t)M * 4, st));
     WX_TRY(gemm_run(p->fc1[l], st));
     WX_TRY(launch_quantize_rows(e->f, WX_DTYPE_BF16, M, ffn, ffn, e->rowmax, 1, e->fq, ffn, e->sa,

@@ -85,6 +85,10 @@ int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, cons
                           void* out, int out_dtype, int64_t rows, int64_t cols, int64_t ld_in,
                           int64_t ld_out, float eps, int mode, int rounding, cudaStream_t st);
 
+int launch_layernorm_quant_rows(const float* in, const float* gamma, const float* beta, int8_t* q,
+                                float* scale, int64_t rows, int64_t cols, int64_t ld_in,
+                                int64_t ld_q, float eps, cudaStream_t st);
+
 // int8 quantisation (quant.cu)
 int launch_absmax_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld,
                        float* out, int64_t out_stride, cudaStream_t st);

@@ -85,6 +85,20 @@ __device__ __forceinline__ uint32_t q8(float x, float sa) {
   return (uint32_t)(__float2int_rn(__fdiv_rn(x, sa)) & 0xFF);
 }
 
+// the per-row divisor and its reciprocal: scale = max / 127 (1 for a zero row)
+struct RowScale {
+  float s, rcp;
+  bool fast;   // s in the range where quant4_i8's FMA division is exact
+};
+__device__ __forceinline__ RowScale row_scale(float m) {
+  RowScale r;
+  r.s = __fdiv_rn(m, 127.0f);
+  if (r.s == 0.0f) r.s = 1.0f;
+  r.rcp = __frcp_rn(r.s);
+  r.fast = div2_rn_safe(r.s);
+  return r;
+}
+
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(32 * kQuantWarps)
     absmax_rows_kernel(const T* __restrict__ in, int64_t rows, int64_t cols, int64_t ld,
@@ -107,31 +121,31 @@ __global__ void __launch_bounds__(32 * kQuantWarps)
   if (row >= rows) return;
   const T* x = in + row * ld;
   const float m = rowmax ? rowmax[row * rowmax_stride] : row_absmax<T, VEC>(x, cols, lane);
-  float sa = __fdiv_rn(m, 127.0f);
-  if (sa == 0.0f) sa = 1.0f;
-  if (lane == 0) scale[row] = sa;
+  const RowScale rs = row_scale(m);
+  if (lane == 0) scale[row] = rs.s;
   int8_t* qr = q + row * ld_q;
   constexpr int V = Vec16<T>::N;
   int64_t c0 = 0;
   if (VEC) {
     const int64_t nv = cols / V;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
+#pragma unroll 4
     for (int64_t i = lane; i < nv; i += 32) {
       float v[V];
       unpack16(__ldg(xv + i), v);
       if constexpr (V == 8) {
         uint2 o;
-        o.x = q8(v[0], sa) | (q8(v[1], sa) << 8) | (q8(v[2], sa) << 16) | (q8(v[3], sa) << 24);
-        o.y = q8(v[4], sa) | (q8(v[5], sa) << 8) | (q8(v[6], sa) << 16) | (q8(v[7], sa) << 24);
+        o.x = quant4_i8(v[0], v[1], v[2], v[3], rs.s, rs.rcp, rs.fast);
+        o.y = quant4_i8(v[4], v[5], v[6], v[7], rs.s, rs.rcp, rs.fast);
         *reinterpret_cast<uint2*>(qr + i * 8) = o;
       } else {
         *reinterpret_cast<uint32_t*>(qr + i * 4) =
-            q8(v[0], sa) | (q8(v[1], sa) << 8) | (q8(v[2], sa) << 16) | (q8(v[3], sa) << 24);
+            quant4_i8(v[0], v[1], v[2], v[3], rs.s, rs.rcp, rs.fast);
       }
     }
     c0 = nv * V;
   }
-  for (int64_t c = c0 + lane; c < cols; c += 32) qr[c] = (int8_t)q8(load_as_f32<T>(x + c), sa);
+  for (int64_t c = c0 + lane; c < cols; c += 32) qr[c] = (int8_t)q8(load_as_f32<T>(x + c), rs.s);
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }

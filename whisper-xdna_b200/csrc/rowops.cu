@@ -776,6 +776,76 @@ __global__ void __launch_bounds__(256) layernorm_fp32_kernel(
   }
 }
 
+// The encoder's fp32 LayerNorm fused with the int8 mode's per-token
+// quantisation of its output (the activation side of q_matmul,
+// bench/probe_int8_decode.py:61-67): the normalised row stays in registers,
+// its max |y| gives scale = max / 127 (1 for a zero row) and q = rint(y /
+// scale). Mean, variance and y follow layernorm_fp32_kernel step for step, so
+// q equals quantising that kernel's fp32 output.
+template <int NV>
+__global__ void __launch_bounds__(256) layernorm_quant_kernel(
+    const float* __restrict__ in, const float* __restrict__ gamma, const float* __restrict__ beta,
+    int8_t* __restrict__ q, int64_t ld_q, float* __restrict__ scale, int64_t rows, int w,
+    int64_t ld_in, float eps) {
+  const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
+  for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
+       row += (int64_t)gridDim.x * warps) {
+    float4 v[NV];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const int c = (i * 32 + lane) * 4;
+      v[i] = c < w ? __ldg(reinterpret_cast<const float4*>(in + row * ld_in + c))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < NV; i++) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = warp_sum(s) / (float)w;
+    float qs = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const int c = (i * 32 + lane) * 4;
+      if (c < w) {
+        const float a = v[i].x - mean, b = v[i].y - mean, d = v[i].z - mean, e = v[i].w - mean;
+        qs += (a * a + b * b) + (d * d + e * e);
+      }
+    }
+    const float rstd = 1.0f / sqrtf(warp_sum(qs) / (float)w + eps);
+    uint32_t mx = 0;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const int c = (i * 32 + lane) * 4;
+      if (c < w) {
+        const float4 g = gamma ? __ldg(reinterpret_cast<const float4*>(gamma + c))
+                               : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float4 b = beta ? __ldg(reinterpret_cast<const float4*>(beta + c))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 t = v[i];
+        v[i] = make_float4((t.x - mean) * rstd * g.x + b.x, (t.y - mean) * rstd * g.y + b.y,
+                           (t.z - mean) * rstd * g.z + b.z, (t.w - mean) * rstd * g.w + b.w);
+        mx = max(mx, max(max(__float_as_uint(v[i].x) & 0x7FFFFFFFu,
+                             __float_as_uint(v[i].y) & 0x7FFFFFFFu),
+                         max(__float_as_uint(v[i].z) & 0x7FFFFFFFu,
+                             __float_as_uint(v[i].w) & 0x7FFFFFFFu)));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sa = __fdiv_rn(__uint_as_float(mx), 127.0f);
+    if (sa == 0.0f) sa = 1.0f;
+    const float rcp = __frcp_rn(sa);
+    const bool fast = div2_rn_safe(sa);
+    if (lane == 0) scale[row] = sa;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const int c = (i * 32 + lane) * 4;
+      if (c < w)
+        *reinterpret_cast<uint32_t*>(q + row * ld_q + c) =
+            quant4_i8(v[i].x, v[i].y, v[i].z, v[i].w, sa, rcp, fast);
+    }
+  }
+}
+
 template <bool IB, bool OB>
 static void launch_ln_fp32(int grid, cudaStream_t st, const void* in, const float* gamma,
                            const float* beta, void* out, int64_t rows, int w, int64_t ld_in,
@@ -992,9 +1062,41 @@ int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, cons
   return check_launch("layernorm_fp32");
 }
 
+int launch_layernorm_quant_rows(const float* in, const float* gamma, const float* beta, int8_t* q,
+                                float* scale, int64_t rows, int64_t cols, int64_t ld_in,
+                                int64_t ld_q, float eps, cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return fail(WX_ERR_INVALID, "layernorm_quant: rows and cols must be > 0");
+  if (!in || !q || !scale) return fail(WX_ERR_INVALID, "layernorm_quant: NULL pointer");
+  if (cols % 4 != 0 || ld_in % 4 != 0 || ld_q % 4 != 0 || ld_in < cols || ld_q < cols ||
+      !aligned16(in) || (reinterpret_cast<uintptr_t>(q) & 3) || (gamma && !aligned16(gamma)) ||
+      (beta && !aligned16(beta)))
+    return fail(WX_ERR_INVALID, "layernorm_quant: cols, ld_in and ld_q must be multiples of 4, "
+                "in, gamma and beta 16-byte aligned, q 4-byte aligned");
+  if (cols > 2048) return fail(WX_ERR_UNSUPPORTED, "layernorm_quant: rows wider than 2048");
+  const int grid = grid_for(rows, 8, 8);
+  const int nv = ((int)cols + 127) / 128, w = (int)cols;
+#define WX_LNQ_CASE(N) \
+  layernorm_quant_kernel<N><<<grid, 256, 0, st>>>(in, gamma, beta, q, ld_q, scale, rows, w, ld_in, eps)
+  if (nv <= 3) WX_LNQ_CASE(3);
+  else if (nv <= 4) WX_LNQ_CASE(4);
+  else if (nv <= 6) WX_LNQ_CASE(6);
+  else if (nv <= 8) WX_LNQ_CASE(8);
+  else if (nv <= 10) WX_LNQ_CASE(10);
+  else WX_LNQ_CASE(16);
+#undef WX_LNQ_CASE
+  return check_launch("layernorm_quant");
+}
+
 }  // namespace wx
 
 extern "C" {
+
+int wx_layernorm_quant_rows(const float* in, const float* gamma, const float* beta, int8_t* q,
+                            float* scale, int64_t rows, int64_t cols, int64_t ld_in, int64_t ld_q,
+                            float eps, void* stream) {
+  return wx::launch_layernorm_quant_rows(in, gamma, beta, q, scale, rows, cols, ld_in, ld_q, eps,
+                                         wx::as_stream(stream));
+}
 
 int wx_gelu_poly4(const void* in, int in_dtype, void* out, int64_t rows, int64_t cols,
                   int64_t ld_in, int64_t ld_out, int rounding, void* stream) {

@@ -48,6 +48,7 @@ SIGNATURES = {
     "wx_gelu4_table": (_i, [_i, _p, _i64]),
     "wx_gemm_bf16": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p]),
     "wx_absmax_rows": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p]),
+    "wx_layernorm_quant_rows": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _p]),
     "wx_quantize_rows": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _p]),
     "wx_gemm_i8": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i,
                         _p, _p]),

@@ -170,6 +170,24 @@ def quantize_rows(x, rowmax=None, q=None, scale=None):
     return q, scale
 
 
+def layer_norm_quant_rows(x, gamma=None, beta=None, eps=1e-5, q=None, scale=None):
+    """fp32 LayerNorm of each row of x quantised per row to int8, in one pass:
+    the same (q, scale) as quantize_rows(layer_norm_rows(x, ..., fp32 out))."""
+    _mat(x, "x", (torch.float32,))
+    rows, cols = x.shape
+    if q is None:
+        q = torch.empty(rows, (cols + 15) // 16 * 16, dtype=torch.int8, device=x.device)[:, :cols]
+    _mat(q, "q", (torch.int8,))
+    if scale is None:
+        scale = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _outvec(scale, rows, "scale")
+    g = _vec(gamma, cols, "gamma")
+    b = _vec(beta, cols, "beta")
+    L.check(L.lib().wx_layernorm_quant_rows(_ptr(x), _ptr(g), _ptr(b), _ptr(q), _ptr(scale), rows,
+                                            cols, x.stride(0), q.stride(0), eps, _stream()))
+    return q, scale
+
+
 def gemm_i8(Aq, Wq, sa, sw, bias=None, residual=None, out=None, epilogue=None, rowmax=None):
     """epilogue((float(Aq @ Wq^T) * sa[:, None]) * sw[None, :]) on the int8
     tensor cores: Aq (M, K) and Wq (N, K) int8 with rows 16-byte aligned, sa
