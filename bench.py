@@ -70,7 +70,6 @@ def arm_config(batch, world, quant="none"):
     if quant != "none":
         cfg["quant"] = (f"{quant}: int8 conv/QKV/out-proj/fc1/fc2 GEMMs with per-token "
                         "activation scales (bench/probe_int8_decode.py:48-74), bf16 attention")
-        cfg["gelu"] = "exact erf (the int8 probe's host GELU)"
     return cfg
 
 
@@ -266,7 +265,7 @@ def run_b200(args, rank, world, local_rank):
     B = args.batch
     W = make_weights_fast(seed=1)
     quant = None if args.quant == "none" else args.quant
-    enc = Encoder(W, max_batch=B, gelu="poly4" if quant is None else "erf", quant=quant)
+    enc = Encoder(W, max_batch=B, gelu="poly4", quant=quant)
     del W
     # per-clip seeded mel, pinned host copy for the end-to-end leg
     g = torch.Generator().manual_seed(1000 + rank)
