@@ -18,10 +18,11 @@
 //              four softmax warps on every SM sub-partition; the two halves
 //              exchange their partial row maxima through shared memory at a
 //              64-thread named barrier once per block and their row sums once
-//              at the end. The tiles take turns on the SFU (A's exponentials of
-//              block j, then B's, then A's of j + 1): while one tile's warps on
-//              a sub-partition compute exponentials, the other's load S, take
-//              the row max and store P.
+//              at the end. Three exponential pairs in four run on the SFU and
+//              one on the FMA pipe (exp2_poly2), and the two tiles' warps
+//              share each sub-partition freely. (Making the tiles take turns
+//              on the SFU paid while every exponential was an SFU one; with a
+//              quarter on the FMA pipe it costs 5%.)
 //
 // Tensor memory (512 columns): S_A double-buffered at columns 0 and 96, S_B at
 // 192 and 288, O_A at 384, O_B at 448. P = exp2(s*c - m) is written back as
@@ -79,7 +80,7 @@ constexpr int kQBytes = kAttBQ * kAttHD * 2;      // 16 KB Q tile
 constexpr int kKVBytes = kAttBK * kAttHD * 2;     // 12 KB K or V tile
 // Q_A, Q_B, the K and V rings, barriers, the row-max exchange (2 tiles x 2
 // parities x 2 halves x 128 rows of fp32)
-constexpr int kAttBarBytes = 512;                // 35 mbarriers and the TMEM address
+constexpr int kAttBarBytes = 512;                // 27 mbarriers and the TMEM address
 constexpr int kAttSmem = 1024 + 2 * kQBytes + 2 * kAttStages * kKVBytes + kAttBarBytes +
                          2 * 2 * 2 * 128 * 4;
 constexpr int kAttTmemCols = 512;
@@ -89,7 +90,7 @@ constexpr int kOCol = 4 * kSBufCols;              // O_A at 384, O_B at 448
 __host__ __device__ constexpr int p_col(int half) { return half ? 64 : 0; }
 constexpr float kRescaleThreshold = 8.0f;         // log2 units
 static_assert(kOCol + 2 * kAttHD <= kAttTmemCols, "tensor memory budget");
-static_assert((1 + 4 * kAttStages + 4 + 4 + 4 + 2 + 8) * 8 + 4 <= kAttBarBytes, "barrier area");
+static_assert((1 + 4 * kAttStages + 4 + 4 + 4 + 2) * 8 + 4 <= kAttBarBytes, "barrier area");
 static_assert(2 * kQBytes % 1024 == 0 && kKVBytes % 1024 == 0, "SW128 tiles 1024-aligned");
 
 template <int N>
@@ -174,10 +175,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   uint64_t* p_full = s_full + 4;                       // [tile][block parity]
   uint64_t* o_done = p_full + 4;                       // [tile][PV parity]
   uint64_t* done = o_done + 4;                         // [tile]
-  // SFU turns of the two tiles' warps on each sub-partition: seq[sub]
-  // completes after tile A's exponentials of a block, seq[4 + sub] after B's
-  uint64_t* seq = done + 2;                            // [direction][sub]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(seq + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
   float* xchg_base = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kAttBarBytes);
 
   const int warp = warp_id(), lane = lane_id();
@@ -202,7 +200,6 @@ __global__ void __launch_bounds__(kAttThreads, 1)
     }
     mbar_init(&done[0], 1);
     mbar_init(&done[1], 1);
-    for (int i = 0; i < 8; i++) mbar_init(&seq[i], 64);
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
@@ -431,17 +428,9 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           sums[(i / 2) & 1] = __fadd2_rn(sums[(i / 2) & 1], make_float2(p0, p1));
         }
       };
-      // SFU turns (seq): tile A's exponentials of block j wait for tile B's of
-      // block j - 1 and tile B's for tile A's of block j. Every wait is
-      // unambiguous: a tile cannot finish two turns before the other has one.
-      if (t == 0) {
-        if (j > 0 && !mbar_wait(&seq[4 + sub], (uint32_t)(j - 1) & 1u, a.err)) ok = false;
-      } else {
-        if (!mbar_wait(&seq[sub], (uint32_t)j & 1u, a.err)) ok = false;
-      }
       if (kvalid >= kAttHalf) make_p(std::false_type());
       else make_p(std::true_type());
-      mbar_arrive(&seq[t * 4 + sub]);
+
       const uint32_t t_p = t_buf + (uint32_t)p_col(half);
       tmem_st16(t_p, pw);
       tmem_st8(t_p + 16, pw + 16);
@@ -470,7 +459,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       l = l * corr + ((sums[0].x + sums[1].x) + (sums[0].y + sums[1].y));
     }
     // tile B's last turn is consumed, so no phase is left pending at exit
-    if (t == 0 && !mbar_wait(&seq[4 + sub], (uint32_t)(nkv - 1) & 1u, a.err)) ok = false;
+
     if (ok) ok = mbar_wait(&o_done[2 * t + ((nkv - 1) & 1)], (uint32_t)((nkv - 1) >> 1) & 1u, a.err);
     // the row sum is the sum of the two halves' sums
     float* lslot = xchg + (nkv & 1) * 256;
