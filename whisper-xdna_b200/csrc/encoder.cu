@@ -204,6 +204,18 @@ static int dalloc(wx_encoder* e, void** p, int64_t bytes) {
   return WX_OK;
 }
 
+// release one of the encoder's allocations before the encoder itself goes
+static void dfree(wx_encoder* e, void** p, int64_t bytes) {
+  if (!*p) return;
+  auto it = std::find(e->allocs.begin(), e->allocs.end(), *p);
+  if (it != e->allocs.end()) {
+    e->allocs.erase(it);
+    e->bytes -= bytes;
+  }
+  cudaFree(*p);
+  *p = nullptr;
+}
+
 static int upload_f32(wx_encoder* e, float* dst, const float* src, int64_t n) {
   if (!src) return fail(WX_ERR_INVALID, "encoder: NULL weight pointer");
   WX_CUDA_TRY(cudaMemcpy(dst, src, (size_t)n * 4, cudaMemcpyHostToDevice));
@@ -632,6 +644,15 @@ int wx_encoder_set_quant(wx_encoder* e, int mode) {
   A((void**)&e->gmax, 16);
   A((void**)&e->stage2, e->stage_n * 4);
   if (s != WX_OK) return s;   // the allocations made are released with the encoder
+  // the bf16 weights are not used in int8 mode
+  dfree(e, (void**)&e->conv1_w, d * k1 * 2);
+  dfree(e, (void**)&e->conv2_w, d * 3 * d * 2);
+  for (LayerW& w : e->L) {
+    dfree(e, (void**)&w.wqkv, 3 * d * d * 2);
+    dfree(e, (void**)&w.wo, d * d * 2);
+    dfree(e, (void**)&w.w1, ffn * d * 2);
+    dfree(e, (void**)&w.w2, ffn * d * 2);
+  }
   e->quant = mode;
   return WX_OK;
 }
