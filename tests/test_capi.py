@@ -89,3 +89,23 @@ def test_invalid_arguments_rejected_before_any_launch(wxlib):
         L.WX_ERR_UNSUPPORTED
     # zero-sized row ops are a no-op success
     assert wxlib.wx_gelu_poly4(nul, 0, nul, 0, 8, 8, 8, 1, nul) == L.WX_OK
+    # int8 path: quantising no rows is a no-op; an empty row has no scale (the
+    # reference's np.abs(A).max(axis=1) raises on it); int8 GEMM rows must be
+    # 16-byte aligned; the encoder handle and mode are checked
+    assert wxlib.wx_quantize_rows(nul, L.WX_DTYPE_F32, 0, 8, 8, nul, 0, nul, 16, nul, nul) == L.WX_OK
+    assert wxlib.wx_quantize_rows(nul, L.WX_DTYPE_F32, 4, 0, 8, nul, 0, nul, 16, nul,
+                                  nul) == L.WX_ERR_INVALID
+    assert wxlib.wx_quantize_rows(nul, 7, 4, 8, 8, nul, 0, nul, 16, nul, nul) == L.WX_ERR_INVALID
+    assert wxlib.wx_absmax_rows(nul, L.WX_DTYPE_BF16, 0, 8, 8, nul, 1, nul) == L.WX_OK
+    assert wxlib.wx_absmax_rows(nul, L.WX_DTYPE_BF16, 4, 8, 4, nul, 1, nul) == L.WX_ERR_INVALID
+    assert wxlib.wx_layernorm_quant_rows(nul, nul, nul, nul, nul, 4, 6, 8, 8, 1e-5,
+                                         nul) == L.WX_ERR_INVALID
+    assert wxlib.wx_gemm_i8(nul, nul, nul, nul, nul, nul, nul, 0, 8, 16, 16, 16, 8, 0, 0, nul,
+                            nul) == L.WX_ERR_INVALID
+    a = ctypes.c_void_p(256)   # not dereferenced: the stride check comes first
+    assert wxlib.wx_gemm_i8(a, a, a, a, nul, nul, a, 32, 32, 24, 24, 24, 32, 0, 0, nul,
+                            nul) == L.WX_ERR_INVALID
+    assert "16-byte" in L.last_error()
+    assert wxlib.wx_gemm_i8(a, a, a, a, nul, nul, a, 32, 32, 32, 32, 32, 32, 0, 9, nul,
+                            nul) == L.WX_ERR_INVALID
+    assert wxlib.wx_encoder_set_quant(nul, L.WX_QUANT_INT8_PERCHAN) == L.WX_ERR_INVALID

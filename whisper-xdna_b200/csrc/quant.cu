@@ -152,7 +152,8 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int launch_absmax_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld,
                        float* out, int64_t out_stride, cudaStream_t st) {
-  if (rows <= 0 || cols <= 0) return fail(WX_ERR_INVALID, "absmax_rows: rows and cols must be > 0");
+  if (rows == 0) return WX_OK;   // nothing to fold
+  if (rows < 0 || cols <= 0) return fail(WX_ERR_INVALID, "absmax_rows: rows >= 0 and cols > 0 required");
   if (!in || !out) return fail(WX_ERR_INVALID, "absmax_rows: NULL pointer");
   if (ld < cols || out_stride < 0) return fail(WX_ERR_INVALID, "absmax_rows: bad ld or out_stride");
   if (in_dtype != WX_DTYPE_BF16 && in_dtype != WX_DTYPE_F32)
@@ -175,7 +176,9 @@ int launch_absmax_rows(const void* in, int in_dtype, int64_t rows, int64_t cols,
 int launch_quantize_rows(const void* in, int in_dtype, int64_t rows, int64_t cols, int64_t ld,
                          const float* rowmax, int64_t rowmax_stride, int8_t* q, int64_t ld_q,
                          float* scale, cudaStream_t st) {
-  if (rows <= 0 || cols <= 0) return fail(WX_ERR_INVALID, "quantize_rows: rows and cols must be > 0");
+  if (rows == 0) return WX_OK;   // nothing to quantise
+  if (rows < 0 || cols <= 0)
+    return fail(WX_ERR_INVALID, "quantize_rows: rows >= 0 and cols > 0 required (an empty row has no scale)");
   if (!in || !q || !scale) return fail(WX_ERR_INVALID, "quantize_rows: NULL pointer");
   if (ld < cols || ld_q < cols || rowmax_stride < 0)
     return fail(WX_ERR_INVALID, "quantize_rows: bad ld, ld_q or rowmax_stride");

@@ -1065,7 +1065,8 @@ int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, cons
 int launch_layernorm_quant_rows(const float* in, const float* gamma, const float* beta, int8_t* q,
                                 float* scale, int64_t rows, int64_t cols, int64_t ld_in,
                                 int64_t ld_q, float eps, cudaStream_t st) {
-  if (rows <= 0 || cols <= 0) return fail(WX_ERR_INVALID, "layernorm_quant: rows and cols must be > 0");
+  if (rows == 0) return WX_OK;
+  if (rows < 0 || cols <= 0) return fail(WX_ERR_INVALID, "layernorm_quant: rows >= 0 and cols > 0 required");
   if (!in || !q || !scale) return fail(WX_ERR_INVALID, "layernorm_quant: NULL pointer");
   if (cols % 4 != 0 || ld_in % 4 != 0 || ld_q % 4 != 0 || ld_in < cols || ld_q < cols ||
       !aligned16(in) || (reinterpret_cast<uintptr_t>(q) & 3) || (gamma && !aligned16(gamma)) ||
