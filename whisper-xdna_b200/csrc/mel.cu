@@ -6,14 +6,17 @@
 // dropped), the power spectrum, a Slaney mel filterbank (0-8 kHz),
 // log10(max(., 1e-10)), a floor 8 below the clip's maximum, then (x + 4) / 4.
 //
-// log_mel_kernel: one CTA per 32 frames of one clip, 8 warps. The 32 frames
-// are staged windowed in shared memory, one frame per lane (rows of 404 floats:
-// 16-byte aligned, and the 16-byte loads of eight consecutive lanes hit
-// distinct banks). Warp w takes DFT bins w, w + 8, ...: every lane reads the
-// same cos/sin row of the DFT matrix (a broadcast through L1; the matrix is
-// 643 KB and stays in L2) and its own frame, in fp32 FMAs. The power spectrum
-// goes to shared memory, each mel band sums its few nonzero filter weights,
-// and the log10 values are written with the block's maximum.
+// log_mel_kernel: one CTA per 32 frames of one clip. The DFT of the 32 frames
+// is a small fp32 GEMM, (32 x 400 windowed samples) x (400 x 416 cos/sin
+// columns), register-tiled: the frames are staged transposed in shared memory,
+// the DFT matrix streams through a double buffer in slices of 16 samples
+// (cp.async), and each of 208 threads accumulates 4 frames x 8 bins (cos and
+// sin: 64 sums), reading one float4 of frames and four float4 of the matrix
+// per sample for 64 FMAs. The matrix is laid out [sample][quarter][bin group]
+// [4] so that the eight bin groups a warp reads sit in consecutive 16-byte
+// units (no bank conflicts). The power spectrum goes to shared memory, each mel
+// band sums its few nonzero filter weights, and the log10 values are written
+// with the block's maximum.
 // log_mel_finalize_kernel: the clip's maximum from the block maxima, then the
 // floor and the affine map, elementwise.
 #include <algorithm>
@@ -28,14 +31,22 @@ namespace wx {
 constexpr int kMelFFT = 400, kMelHop = 160, kMelBins = 201, kMelFrames = 3000;
 constexpr int64_t kMelWindow = 480000;               // 30 s at 16 kHz
 constexpr int kMelFB = 32;                           // frames per CTA
-constexpr int kMelRow = 404;                         // floats per staged frame
 constexpr int kMelBlocks = (kMelFrames + kMelFB - 1) / kMelFB;   // 94 per clip
-constexpr int kMelThreads = 256;
-constexpr int kMelSmem = (kMelFB * kMelRow + kMelFB * kMelBins + 8) * 4;
+constexpr int kMelThreads = 224;                     // 7 warps; 208 compute threads
+constexpr int kMelGroups = 26;                       // bin groups of 8 (208 >= 201 bins)
+constexpr int kMelCompute = 8 * kMelGroups;          // 8 frame groups of 4 x 26 bin groups
+constexpr int kMelKS = 16;                           // samples per DFT-matrix slice
+constexpr int kMelXT = 36;                           // floats per transposed sample row
+constexpr int kMelSlice = kMelKS * 4 * kMelGroups * 4;   // floats per slice (26.6 KB)
+// shared memory: frames transposed [400][36], two matrix slices, 8 maxima; the
+// power spectrum [32][201] reuses the slices after the GEMM
+constexpr int kMelSmem = (kMelFFT * kMelXT + 2 * kMelSlice + 8) * 4;
+static_assert(kMelFB * kMelBins <= 2 * kMelSlice, "power spectrum fits the slice buffers");
+static_assert(kMelFFT % kMelKS == 0, "whole slices");
 
 struct MelTables {
   int n_mels = 0, maxw = 0;
-  float *dcos = nullptr, *dsin = nullptr, *window = nullptr, *fw = nullptr;
+  float *dft = nullptr, *window = nullptr, *fw = nullptr;   // dft: [400][4][26][4]
   int *fstart = nullptr, *flen = nullptr;
 };
 
@@ -81,15 +92,21 @@ static int mel_tables(int n_mels, MelTables** out) {
   if (dev >= 64) return fail(WX_ERR_UNSUPPORTED, "device index %d >= 64", dev);
   std::lock_guard<std::mutex> lk(g_mel_mu);
   MelTables& t = g_mel[dev][n_mels == 128];
-  if (!t.dcos) {
-    std::vector<float> c((size_t)kMelBins * kMelFFT), s(c.size()), win(kMelFFT);
+  if (!t.dft) {
+    // DFT matrix: element [n][q][g][e] is cos (q = 0, 1) or sin (q = 2, 3) of
+    // 2 pi k n / 400 for bin k = 8 g + 4 (q & 1) + e; bins past 200 are zero
+    std::vector<float> dft((size_t)kMelFFT * 4 * kMelGroups * 4, 0.0f), win(kMelFFT);
     const double two_pi = 6.283185307179586;
-    for (int k = 0; k < kMelBins; k++)
-      for (int n = 0; n < kMelFFT; n++) {
-        const double a = two_pi * ((k * n) % kMelFFT) / kMelFFT;   // exact reduction
-        c[(size_t)k * kMelFFT + n] = (float)std::cos(a);
-        s[(size_t)k * kMelFFT + n] = (float)std::sin(a);
-      }
+    for (int n = 0; n < kMelFFT; n++)
+      for (int q = 0; q < 4; q++)
+        for (int g = 0; g < kMelGroups; g++)
+          for (int e = 0; e < 4; e++) {
+            const int k = 8 * g + 4 * (q & 1) + e;
+            if (k >= kMelBins) continue;
+            const double a = two_pi * ((k * n) % kMelFFT) / kMelFFT;   // exact reduction
+            dft[(((size_t)n * 4 + q) * kMelGroups + g) * 4 + e] =
+                (float)(q < 2 ? std::cos(a) : std::sin(a));
+          }
     for (int n = 0; n < kMelFFT; n++) win[n] = (float)(0.5 - 0.5 * std::cos(two_pi * n / kMelFFT));
     const std::vector<double> fb = slaney_filters(n_mels);
     std::vector<int> st(n_mels), len(n_mels);
@@ -109,14 +126,12 @@ static int mel_tables(int n_mels, MelTables** out) {
     MelTables nt;
     nt.n_mels = n_mels;
     nt.maxw = maxw;
-    WX_CUDA_TRY(cudaMalloc(&nt.dcos, c.size() * 4));
-    WX_CUDA_TRY(cudaMalloc(&nt.dsin, s.size() * 4));
+    WX_CUDA_TRY(cudaMalloc(&nt.dft, dft.size() * 4));
     WX_CUDA_TRY(cudaMalloc(&nt.window, kMelFFT * 4));
     WX_CUDA_TRY(cudaMalloc(&nt.fw, fw.size() * 4));
     WX_CUDA_TRY(cudaMalloc(&nt.fstart, n_mels * 4));
     WX_CUDA_TRY(cudaMalloc(&nt.flen, n_mels * 4));
-    WX_CUDA_TRY(cudaMemcpy(nt.dcos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
-    WX_CUDA_TRY(cudaMemcpy(nt.dsin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+    WX_CUDA_TRY(cudaMemcpy(nt.dft, dft.data(), dft.size() * 4, cudaMemcpyHostToDevice));
     WX_CUDA_TRY(cudaMemcpy(nt.window, win.data(), kMelFFT * 4, cudaMemcpyHostToDevice));
     WX_CUDA_TRY(cudaMemcpy(nt.fw, fw.data(), fw.size() * 4, cudaMemcpyHostToDevice));
     WX_CUDA_TRY(cudaMemcpy(nt.fstart, st.data(), n_mels * 4, cudaMemcpyHostToDevice));
@@ -127,22 +142,39 @@ static int mel_tables(int n_mels, MelTables** out) {
   return WX_OK;
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __global__ void __launch_bounds__(kMelThreads) log_mel_kernel(
     const float* __restrict__ audio, int64_t ld_audio, int64_t n_samples,
-    const float* __restrict__ dcos, const float* __restrict__ dsin,
-    const float* __restrict__ window, const int* __restrict__ fstart,
-    const int* __restrict__ flen, const float* __restrict__ fw, int maxw, int n_mels,
-    float* __restrict__ out, float* __restrict__ block_max) {
+    const float* __restrict__ dft, const float* __restrict__ window,
+    const int* __restrict__ fstart, const int* __restrict__ flen, const float* __restrict__ fw,
+    int maxw, int n_mels, float* __restrict__ out, float* __restrict__ block_max) {
   extern __shared__ __align__(16) float msm[];
-  float* frames = msm;                          // [32][404]
-  float* power = msm + kMelFB * kMelRow;        // [32][201]
-  float* wmax = power + kMelFB * kMelBins;      // [8]
+  float* xt = msm;                              // [400][36]: sample n, frame f
+  float* slab = msm + kMelFFT * kMelXT;         // 2 slices of the DFT matrix
+  float* power = slab;                          // [32][201], after the GEMM
+  float* wmax = slab + 2 * kMelSlice;           // [7]
   const int b = blockIdx.y, f0 = blockIdx.x * kMelFB;
-  const int lane = lane_id(), warp = warp_id();
+  const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   const float* a = audio + (int64_t)b * ld_audio;
-  // windowed frames: sample j of the 30 s window is audio[j] below n_samples
-  // and 0 above (pad_or_trim); positions outside the window reflect
-  for (int i = threadIdx.x; i < kMelFB * kMelFFT; i += kMelThreads) {
+  auto load_slice = [&](int sl, int buf) {
+    const float4* src = reinterpret_cast<const float4*>(dft + (size_t)sl * kMelSlice);
+    float4* dst = reinterpret_cast<float4*>(slab + buf * kMelSlice);
+    for (int i = tid; i < kMelSlice / 4; i += kMelThreads) cp_async16(dst + i, src + i);
+    cp_async_commit();
+  };
+  load_slice(0, 0);
+  // windowed frames, transposed: sample j of the 30 s window is audio[j] below
+  // n_samples and 0 above (pad_or_trim); positions outside the window reflect
+  for (int i = tid; i < kMelFB * kMelFFT; i += kMelThreads) {
     const int f = i / kMelFFT, n = i - f * kMelFFT;
     float v = 0.0f;
     if (f0 + f < kMelFrames) {
@@ -151,29 +183,56 @@ __global__ void __launch_bounds__(kMelThreads) log_mel_kernel(
       if (j >= kMelWindow) j = 2 * (kMelWindow - 1) - j;
       v = (j < n_samples ? __ldg(a + j) : 0.0f) * __ldg(window + n);
     }
-    frames[f * kMelRow + n] = v;
+    xt[n * kMelXT + f] = v;
   }
-  __syncthreads();
-  // |DFT|^2 of this lane's frame at the warp's bins
-  const float4* xr = reinterpret_cast<const float4*>(frames + lane * kMelRow);
-  for (int k = warp; k < kMelBins; k += kMelThreads / 32) {
-    const float4* cr = reinterpret_cast<const float4*>(dcos + k * kMelFFT);
-    const float4* sr = reinterpret_cast<const float4*>(dsin + k * kMelFFT);
-    float re0 = 0.0f, re1 = 0.0f, im0 = 0.0f, im1 = 0.0f;
-#pragma unroll 4
-    for (int q = 0; q < kMelFFT / 4; q++) {
-      const float4 x = xr[q], c = __ldg(cr + q), s = __ldg(sr + q);
-      re0 = fmaf(x.x, c.x, re0);
-      re1 = fmaf(x.y, c.y, re1);
-      re0 = fmaf(x.z, c.z, re0);
-      re1 = fmaf(x.w, c.w, re1);
-      im0 = fmaf(x.x, s.x, im0);
-      im1 = fmaf(x.y, s.y, im1);
-      im0 = fmaf(x.z, s.z, im0);
-      im1 = fmaf(x.w, s.w, im1);
+  // DFT: thread t < 208 takes frames 4 (t % 8) .. + 3 and bins 8 (t / 8) .. + 7
+  const int fg = tid & 7, bg = tid >> 3;
+  const bool active = tid < kMelCompute;
+  float acc[4][16];
+#pragma unroll
+  for (int f = 0; f < 4; f++)
+#pragma unroll
+    for (int c = 0; c < 16; c++) acc[f][c] = 0.0f;
+  constexpr int nsl = kMelFFT / kMelKS;
+  for (int sl = 0; sl < nsl; sl++) {
+    if (sl + 1 < nsl) {
+      load_slice(sl + 1, (sl + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    const float re = re0 + re1, im = im0 + im1;
-    power[lane * kMelBins + k] = re * re + im * im;
+    __syncthreads();   // slice sl (and, the first time, the frames) visible to all
+    if (active) {
+      const float* d = slab + (sl & 1) * kMelSlice + bg * 4;
+#pragma unroll 4
+      for (int kk = 0; kk < kMelKS; kk++) {
+        const float4 x = *reinterpret_cast<const float4*>(xt + (sl * kMelKS + kk) * kMelXT + fg * 4);
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float4 w = *reinterpret_cast<const float4*>(d + (kk * 4 + q) * kMelGroups * 4);
+#pragma unroll
+          for (int f = 0; f < 4; f++) {
+            acc[f][4 * q] = fmaf(xs[f], w.x, acc[f][4 * q]);
+            acc[f][4 * q + 1] = fmaf(xs[f], w.y, acc[f][4 * q + 1]);
+            acc[f][4 * q + 2] = fmaf(xs[f], w.z, acc[f][4 * q + 2]);
+            acc[f][4 * q + 3] = fmaf(xs[f], w.w, acc[f][4 * q + 3]);
+          }
+        }
+      }
+    }
+    __syncthreads();   // every thread is done with this slice before it is refilled
+  }
+  // |X|^2: cos sums in columns 0-7, sin sums in 8-15
+  if (active) {
+#pragma unroll
+    for (int f = 0; f < 4; f++)
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const int k = 8 * bg + e;
+        if (k < kMelBins)
+          power[(4 * fg + f) * kMelBins + k] = acc[f][e] * acc[f][e] + acc[f][8 + e] * acc[f][8 + e];
+      }
   }
   __syncthreads();
   // mel bands, log10, the block's maximum
@@ -278,8 +337,8 @@ extern "C" int wx_log_mel(const float* audio, int64_t batch, int64_t n_samples, 
   cudaStream_t st = as_stream(stream);
   const int64_t n_used = std::min<int64_t>(n_samples, kMelWindow);
   log_mel_kernel<<<dim3(kMelBlocks, (unsigned)batch), kMelThreads, kMelSmem, st>>>(
-      audio, ld_audio, n_used, t->dcos, t->dsin, t->window, t->fstart, t->flen, t->fw, t->maxw,
-      n_mels, mel_out, bmax);
+      audio, ld_audio, n_used, t->dft, t->window, t->fstart, t->flen, t->fw, t->maxw, n_mels,
+      mel_out, bmax);
   WX_TRY(check_launch("log_mel"));
   log_mel_finalize_kernel<<<dim3(16, (unsigned)batch), 256, 0, st>>>(mel_out, bmax, n_mels);
   return check_launch("log_mel_finalize");
