@@ -35,7 +35,7 @@ N_MELS, D, N_HEAD, N_LAYER, FFN, CTX = 128, 1280, 20, 32, 5120, 1500
 # DRAM bytes (read + write) of one attention launch per clip, measured by ncu
 # on a 4-clip launch (profiles/attention_ncu_b4.md: 46.14 MB read, 0.28 MB
 # written); Q, K and V are read once, O stays in L2 at that size.
-ATTN_DRAM_BYTES_PER_CLIP = (46.176e6 + 0.344e6) / 4
+ATTN_DRAM_BYTES_PER_CLIP = (46.173e6 + 0.453e6) / 4
 FLOP_PER_CLIP = (N_LAYER * (8 * CTX * D * D + 4 * CTX * D * FFN + 4 * CTX * CTX * D)
                  + 2 * (2 * CTX) * (3 * N_MELS) * D + 2 * CTX * (3 * D) * D)
 
