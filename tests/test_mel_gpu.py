@@ -89,3 +89,29 @@ def test_bad_arguments(cuda):
         L.check(L.lib().wx_log_mel(a.data_ptr(), 1, 100, 50, 80, out.data_ptr(), None))
     with pytest.raises(L.WxError):
         L.check(L.lib().wx_log_mel(a.data_ptr(), 1, 100, 100, 64, out.data_ptr(), None))
+
+
+def test_encode_recording_equals_windows_one_by_one(cuda):
+    """A 67 s recording: three 30 s windows (the last 7 s, zero-padded) as one
+    batch through log-mel and the encoder equal the windows done one by one,
+    as the reference's transcribe loop does them (serve/npu_stt_server.py:
+    421-431 and _window :331-342), at a reduced audio_ctx of 512."""
+    import encoder_ref as R
+    from wxb200 import audio as A
+    from wxb200.encoder import Encoder
+    rec = np.concatenate([M.synthetic_audio(30, 1), M.synthetic_audio(30, 2, "noise"),
+                          M.synthetic_audio(7, 3)]).astype(np.float32)
+    W = R.make_weights("tiny", seed=3, n_layer=2)
+    enc = Encoder(W, n_layer=2, n_head=6, max_batch=2)     # two forwards: 2 + 1 windows
+    try:
+        feats, cut = A.encode_recording(enc, rec, ctx=512)
+        assert cut == 0.0 and tuple(feats.shape) == (3, 512, 384)
+        for i, off in enumerate(A.split_windows(rec.size)[0]):
+            mel = A.log_mel_spectrogram(A.pad_or_trim(rec[off:off + A.N_SAMPLES]), 80,
+                                        device="cuda")
+            one = enc.forward(mel[:, :1024].contiguous())
+            assert torch.equal(one, feats[i]), i
+        feats2, cut2 = A.encode_recording(enc, rec, ctx=512, max_windows=2)
+        assert cut2 == pytest.approx(7.0) and torch.equal(feats2, feats[:2])
+    finally:
+        enc.close()
