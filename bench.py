@@ -48,8 +48,6 @@ def parse():
     ap.add_argument("--batch", type=int, default=64, help="clips per GPU per step")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-layers", type=int, default=2,
-                    help="layers in the bounded CPU sample")
     ap.add_argument("--quant", choices=["none", "int8-perchan", "int8-pertensor"],
                     default="none",
                     help="int8 projection/MLP mode (the reference's int8 probe); not the "
@@ -75,27 +73,25 @@ def arm_config(batch, world, quant="none"):
 
 # ------------------------------------------------------------------ CPU side
 
-def cpu_sample(n_layers, seed=1):
-    """Time the oracle port of the reference's numpy encoder on one clip:
-    frontend, n_layers blocks, ln_post; extrapolate to 32 layers.
+def cpu_clips(W, min_seconds=10.0, max_clips=3, first_seed=0):
+    """Time the oracle port of the reference's numpy encoder on whole large-v3
+    clips (frontend, 32 layers, ln_post; ctx 1500) until at least
+    min_seconds have passed or max_clips are done.
     Returns (clips_per_s, seconds_spent, description)."""
     sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
     import encoder_ref as R
-    W = R.make_weights("large-v3", seed=seed, n_layer=n_layers)
-    mel = R.make_mel(N_MELS, 2 * CTX, seed=0)
     t0 = time.perf_counter()
-    R.encoder_np(W, mel, n_layer=0, n_head=N_HEAD)          # frontend + ln_post
-    t1 = time.perf_counter()
-    R.encoder_np(W, mel, n_layer=n_layers, n_head=N_HEAD)
-    t2 = time.perf_counter()
-    front = t1 - t0
-    per_layer = ((t2 - t1) - front) / n_layers
-    clip_s = front + N_LAYER * per_layer
-    desc = (f"1 clip of large-v3 ctx 1500: frontend+ln_post ({front:.2f} s) and "
-            f"{n_layers} layers ({per_layer:.2f} s/layer) timed, extrapolated to "
-            f"32 layers = {clip_s:.1f} s/clip")
-    return 1.0 / clip_s, t2 - t0, desc
+    n = 0
+    while n < max_clips:
+        mel = R.make_mel(N_MELS, 2 * CTX, seed=first_seed + n)
+        R.encoder_np(W, mel, n_layer=N_LAYER, n_head=N_HEAD)
+        n += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
+    spent = time.perf_counter() - t0
+    desc = (f"{n} whole clip{'s' if n > 1 else ''} of large-v3 ctx 1500 (frontend, 32 layers, "
+            f"ln_post), {spent / n:.1f} s per clip")
+    return n / spent, spent, desc
 
 
 def cpu_cores():
@@ -120,13 +116,15 @@ def run_reference(args, rank):
         threadpool_limits(limits=n)
     except Exception:
         pass
-    for _ in range(args.warmup):
-        cpu_sample(1)
-    vals, spent, desc = [], 0.0, ""
-    for _ in range(args.steps):
-        v, s, desc = cpu_sample(args.cpu_layers)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import encoder_ref as R
+    W = make_weights_fast(seed=1)
+    for i in range(args.warmup):   # one layer per warm-up step
+        R.encoder_np(W, R.make_mel(N_MELS, 2 * CTX, seed=100 + i), n_layer=1, n_head=N_HEAD)
+    vals, desc = [], ""
+    for i in range(args.steps):    # one whole clip per step
+        v, _, desc = cpu_clips(W, min_seconds=0.0, max_clips=1, first_seed=i)
         vals.append(v)
-        spent += s
     value = statistics.median(vals)
     out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
@@ -266,7 +264,9 @@ def run_b200(args, rank, world, local_rank):
     W = make_weights_fast(seed=1)
     quant = None if args.quant == "none" else args.quant
     enc = Encoder(W, max_batch=B, gelu="poly4", quant=quant)
-    del W
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline and quant is None
+    if not want_cpu:
+        del W
     # per-clip seeded mel, pinned host copy for the end-to-end leg
     g = torch.Generator().manual_seed(1000 + rank)
     mel_host = torch.empty(B, N_MELS, 2 * CTX, pin_memory=True)
@@ -333,10 +333,12 @@ def run_b200(args, rank, world, local_rank):
                 "whole_step": {"achieved": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12,
                                "frac": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12
                                / peaks["bf16_tflops"]}}
-        if world == 1 and not args.no_cpu_baseline and quant is None:
-            v, spent, desc = cpu_sample(args.cpu_layers)
+        if want_cpu:
+            v, spent, desc = cpu_clips(W, min_seconds=10.0, max_clips=3)
+            del W
             cpu = {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
-                   "sample": desc + f"; {spent:.1f} s of CPU time"}
+                   "sample": desc + f"; {spent:.1f} s of CPU time, the oracle port of the "
+                                    "reference's numpy encoder, all BLAS threads"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
