@@ -53,13 +53,18 @@ __device__ __forceinline__ float gelu_erf(float x) {
 __device__ __forceinline__ void dequant32(const GemmArgs& a, float s_row, int n,
                                           const uint32_t (&acc)[32], float (&v)[32]) {
   if (n + 32 <= a.N) {
+    // packed fp32 pairs: each product rounded on its own, as fmul.rn
+    const float2 sr = make_float2(s_row, s_row);
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       const float4 w = __ldg(reinterpret_cast<const float4*>(a.sw + n + j));
-      v[j] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j]), s_row), w.x);
-      v[j + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j + 1]), s_row), w.y);
-      v[j + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j + 2]), s_row), w.z);
-      v[j + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)acc[j + 3]), s_row), w.w);
+      const float2 p0 = __fmul2_rn(__fmul2_rn(make_float2(__int2float_rn((int)acc[j]),
+                                                          __int2float_rn((int)acc[j + 1])), sr),
+                                   make_float2(w.x, w.y));
+      const float2 p1 = __fmul2_rn(__fmul2_rn(make_float2(__int2float_rn((int)acc[j + 2]),
+                                                          __int2float_rn((int)acc[j + 3])), sr),
+                                   make_float2(w.z, w.w));
+      v[j] = p0.x; v[j + 1] = p0.y; v[j + 2] = p1.x; v[j + 3] = p1.y;
     }
   } else {
 #pragma unroll
@@ -225,7 +230,9 @@ __device__ __forceinline__ void add_bias32(const GemmArgs& a, int n, float (&v)[
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       const float4 b = __ldg(reinterpret_cast<const float4*>(a.bias + n + j));
-      v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+      const float2 s0 = __fadd2_rn(make_float2(v[j], v[j + 1]), make_float2(b.x, b.y));
+      const float2 s1 = __fadd2_rn(make_float2(v[j + 2], v[j + 3]), make_float2(b.z, b.w));
+      v[j] = s0.x; v[j + 1] = s0.y; v[j + 2] = s1.x; v[j + 3] = s1.y;
     }
   } else {
 #pragma unroll
