@@ -23,8 +23,8 @@
 // quantised once per output channel (or per weight matrix, per q/k/v and per
 // fc1 column chunk of prepare_mlp_chunks for "pertensor"); each GEMM's
 // activation rows are quantised per token right before it:
-//   im2col (bf16) -> quantise -> conv GEMM          LN (fp32) -> quantise -> QKV
-//   attention (bf16) -> quantise -> out-proj          LN (fp32) -> quantise -> fc1
+//   im2col (bf16) -> quantise -> conv GEMM          LN + quantise (one kernel) -> QKV
+//   attention (bf16) -> quantise -> out-proj          LN + quantise (one kernel) -> fc1
 //   fc1 + GELU (bf16, with max |row| by atomics) -> quantise -> fc2
 // Attention itself stays bf16 (the probe keeps it in fp32: E.np_matmul).
 #include <algorithm>

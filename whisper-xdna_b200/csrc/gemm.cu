@@ -18,6 +18,12 @@
 // N-fastest so the CTAs in flight share A tiles through L2; the weights
 // (<= 13 MB per GEMM) stay L2-resident.
 //
+// Large problems run gemm2_bf16_kernel on CTA pairs (tcgen05 cta_group::2,
+// 256 x 256 tiles), whose epilogue goes through shared memory and TMA tensor
+// stores (and TMA loads of the residual). Both kernels are templated on I8:
+// int8 A and B (kind::i8, s32 accumulator) with the dequantising epilogue of
+// the int8 mode, (float(acc) * sa[row]) * sw[col].
+//
 // It replaces the whole-array AIE GEMM the reference drives through
 // RawRT.matmul / mm_start / mm_finish (src/rawxrt.py:926-996); its bias fold
 // (ones column on A, bias row on B, src/rawxrt.py:352-371) becomes a bias
