@@ -256,7 +256,7 @@ __device__ __forceinline__ void add_bias32(const GemmArgs& a, int n, float (&v)[
 // the buffer and adds it. s_row: the row's int8 scale (I8). Returns, for the
 // bf16 outputs, max |value| over the chunk's columns inside N as bf16
 // magnitude bits (0 otherwise).
-template <int EPI, bool I8>
+template <int EPI, bool I8, bool SEQ>
 __device__ __forceinline__ uint32_t epi_chunk_to_smem(const GemmArgs& a, uint32_t t_col, int n,
                                                       uint8_t* rowp, int lane, float s_row) {
   const int sw = lane & 7;
@@ -283,19 +283,28 @@ __device__ __forceinline__ uint32_t epi_chunk_to_smem(const GemmArgs& a, uint32_
     }
     return 0u;
   } else {
+    // SEQ: one half's columns at a time (fewer live registers at 576 threads);
+    // otherwise both halves' loads in flight together
     uint32_t r0[32], r1[32];
-    tmem_ld32(t_col, r0);
-    tmem_ld32(t_col + 32, r1);
-    tmem_wait_ld();
+    if constexpr (!SEQ) {
+      tmem_ld32(t_col, r0);
+      tmem_ld32(t_col + 32, r1);
+      tmem_wait_ld();
+    }
     uint32_t mx = 0;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
+      if constexpr (SEQ) {
+        tmem_ld32(t_col + 32 * h, r0);
+        tmem_wait_ld();
+      }
+      const uint32_t (&r)[32] = (SEQ || h == 0) ? r0 : r1;
       float v[32];
       if constexpr (I8) {
-        dequant32(a, s_row, n + 32 * h, h ? r1 : r0, v);
+        dequant32(a, s_row, n + 32 * h, r, v);
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(h ? r1[j] : r0[j]);
+        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
       }
       add_bias32(a, n + 32 * h, v);
       uint32_t w[16];
@@ -514,14 +523,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 constexpr int kGemm2ABytes = 128 * kGemmBK * 2;                   // 16 KB
 constexpr int kGemm2BBytes = 128 * kGemmBK * 2;                   // 16 KB (half of N=256)
 constexpr int kGemm2StageBytes = kGemm2ABytes + kGemm2BBytes;
-constexpr int kGemm2EpiBytes = (kGemmEpiThreads / 32) * 2 * kEpiBufBytes;
+constexpr int kGemm2EpiBytes = 64 * 1024;          // staging buffers of the TMA epilogue
 constexpr int kGemm2BarBytes = 512;
-template <int EPI>
+template <int EPI, bool I8>
 struct Gemm2Cfg {
   static constexpr int STAGES = TmaEpi<EPI>::kOn ? 5 : 6;
+  // Epilogue warps: 8 (two per sub-partition, each 32 rows x 128 columns of a
+  // tile, two 4 KB staging buffers each), or 16 for the int8 GELU epilogues
+  // (32 rows x 64 columns, one buffer each): at the int8 MMA rate the GELU
+  // epilogue of fc1 is latency-bound with two warps per sub-partition.
+  static constexpr bool kGeluOut = EPI == WX_EPI_BF16_GELU || EPI == WX_EPI_BF16_GELU_ERF;
+  static constexpr int EPI_WARPS = (I8 && kGeluOut) ? 16 : 8;
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int NBUF = TmaEpi<EPI>::kOn ? kGemm2EpiBytes / (EPI_WARPS * kEpiBufBytes) : 0;
   static constexpr int EPI_BYTES = TmaEpi<EPI>::kOn ? kGemm2EpiBytes : 0;
   static constexpr int SMEM = STAGES * kGemm2StageBytes + EPI_BYTES + 1024 + kGemm2BarBytes;
   static_assert(SMEM <= 232448, "2-SM GEMM shared memory");
+  static_assert(!TmaEpi<EPI>::kOn || NBUF >= 1, "a staging buffer per epilogue warp");
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -606,12 +624,12 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 }
 
 template <int EPI, bool I8>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Cfg<EPI, I8>::THREADS, 1)
     gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC,
                       const __grid_constant__ CUtensorMap tmR, const GemmArgs a) {
-  using Cfg = Gemm2Cfg<EPI>;
+  using Cfg = Gemm2Cfg<EPI, I8>;
   constexpr int S = Cfg::STAGES;
   constexpr int kKElems = I8 ? 2 * kGemmBK : kGemmBK;   // elements per 128-byte K step
   constexpr int BN = 256;
@@ -627,9 +645,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint64_t* tfull = bars + 2 * S;   // [2]
   uint64_t* tempty = tfull + 2;     // [2], used in the leader
   uint64_t* done = tempty + 2;
-  uint64_t* rfull = done + 1;       // [8 warps][2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + 2 * (kGemmEpiThreads / 32));
-  static_assert((2 * S + 5 + 2 * (kGemmEpiThreads / 32)) * 8 + 4 <= kGemm2BarBytes, "barriers");
+  constexpr int EW = Cfg::EPI_WARPS, NB = Cfg::NBUF > 0 ? Cfg::NBUF : 1;
+  uint64_t* rfull = done + 1;       // [EW warps][NB buffers]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + EW * NB);
+  static_assert((2 * S + 5 + EW * NB) * 8 + 4 <= kGemm2BarBytes, "barriers");
 
   const int warp = warp_id(), lane = lane_id();
   const uint32_t rank = cluster_rank();
@@ -641,10 +660,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 2 * (kGemmEpiThreads / 32));
+      mbar_init(&tempty[b], 2 * EW);
     }
     mbar_init(done, 1);
-    for (int i = 0; i < 2 * (kGemmEpiThreads / 32); i++) mbar_init(&rfull[i], 1);
+    for (int i = 0; i < EW * NB; i++) mbar_init(&rfull[i], 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -714,34 +733,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       mbar_wait_for(done, 0, kWaitTimeoutNs);
     }
   } else if constexpr (TmaEpi<EPI>::kOn) {
-    // ---------------- epilogue through shared memory + TMA stores: warps 2..9
-    constexpr int kCols = TmaEpi<EPI>::kCols, kChunks = (BN / 2) / kCols;
-    const int sub = warp & 3;          // TMEM lanes 32*sub .. 32*sub+31
-    const int half = (warp - 2) >> 2;  // column half of the tile
-    uint8_t* ebuf = sE + (warp - 2) * 2 * kEpiBufBytes;
-    uint64_t* rf = rfull + 2 * (warp - 2);
+    // ---------------- epilogue through shared memory + TMA stores: warps 2..17
+    constexpr int kCols = TmaEpi<EPI>::kCols;      // columns per staged chunk
+    constexpr int kPartCols = BN / (EW / 4);       // columns per warp: 64
+    constexpr int kChunks = kPartCols / kCols;     // 1 (bf16) or 2 (fp32) per tile
+    const int sub = warp & 3;                      // TMEM lanes 32*sub .. 32*sub+31
+    const int part = (warp - 2) >> 2;              // column part of the tile
+    uint8_t* ebuf = sE + (warp - 2) * NB * kEpiBufBytes;
+    uint64_t* rf = rfull + NB * (warp - 2);
     const int row_off = (int)rank * 128 + sub * 32;
     // this warp's chunks of a tile: a prefix of kChunks (none past M or N)
     auto chunks_of = [&](int tile) -> int {
-      const int r0 = (tile / nnb) * 256 + row_off, c0 = (tile % nnb) * BN + half * (BN / 2);
+      const int r0 = (tile / nnb) * 256 + row_off, c0 = (tile % nnb) * BN + part * kPartCols;
       if (r0 >= a.M || c0 >= a.N) return 0;
       return min(kChunks, (a.N - c0 + kCols - 1) / kCols);
     };
-    // residual loads (lane 0) run two chunks ahead, across tiles
+    // residual loads (lane 0) run NB chunks ahead, across tiles
     int lt = pair, lc = 0;
     uint32_t lk = 0;
     auto load_next = [&]() {
       while (lt < a.num_tiles && lc >= chunks_of(lt)) { lt += npairs; lc = 0; }
       if (lt >= a.num_tiles) return;
-      const uint32_t b = lk & 1;
+      const uint32_t b = lk % NB;
       mbar_arrive_expect_tx(&rf[b], kEpiBufBytes);
       tma_load_2d(&tmR, &rf[b], ebuf + b * kEpiBufBytes,
-                  (lt % nnb) * BN + half * (BN / 2) + lc * kCols, (lt / nnb) * 256 + row_off);
+                  (lt % nnb) * BN + part * kPartCols + lc * kCols, (lt / nnb) * 256 + row_off);
       lc++;
       lk++;
     };
     if constexpr (EPI == WX_EPI_F32_RESID) {
-      if (lane == 0) { load_next(); load_next(); }
+      if (lane == 0)
+        for (int i = 0; i < NB; i++) load_next();
     }
     int acc = 0;
     uint32_t acc_phase = 0, k = 0;
@@ -750,24 +772,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const int nc = chunks_of(tile);
-      const int r0 = (tile / nnb) * 256 + row_off, c0 = (tile % nnb) * BN + half * (BN / 2);
+      const int r0 = (tile / nnb) * 256 + row_off, c0 = (tile % nnb) * BN + part * kPartCols;
       const uint32_t t_row = tmem_base + ((uint32_t)(sub * 32) << 16) +
-                             (uint32_t)(acc * BN + half * (BN / 2));
+                             (uint32_t)(acc * BN + part * kPartCols);
       const int row = r0 + lane;
       float s_row = 0.0f;
       if constexpr (I8) s_row = row < a.M ? a.sa[row] : 0.0f;
       uint32_t mx = 0;
       for (int c = 0; c < nc; c++, k++) {
-        uint8_t* buf = ebuf + (k & 1) * kEpiBufBytes;
+        uint8_t* buf = ebuf + (k % NB) * kEpiBufBytes;
         if constexpr (EPI == WX_EPI_F32_RESID) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&rf[k & 1], (k >> 1) & 1, a.err));
+          ok = __all_sync(0xffffffffu, mbar_wait(&rf[k % NB], (k / NB) & 1, a.err));
           if (!ok) break;
         } else {
-          if (lane == 0) bulk_wait_group_read<1>();   // the store of chunk k-2 has read buf
+          if (lane == 0) bulk_wait_group_read<NB - 1>();   // the store of chunk k-NB has read buf
           __syncwarp();
         }
-        mx = max(mx, epi_chunk_to_smem<EPI, I8>(a, t_row + (uint32_t)(c * kCols), c0 + c * kCols,
-                                                 buf + lane * 128, lane, s_row));
+        mx = max(mx, epi_chunk_to_smem<EPI, I8, (EW > 8)>(a, t_row + (uint32_t)(c * kCols),
+                                                           c0 + c * kCols, buf + lane * 128,
+                                                           lane, s_row));
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -1040,7 +1063,7 @@ static int set_attr_pair_t() {
   if (dev < 64 && done[dev]) return WX_OK;
   WX_CUDA_TRY(cudaFuncSetAttribute(gemm2_bf16_kernel<EPI, I8>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   Gemm2Cfg<EPI>::SMEM));
+                                   Gemm2Cfg<EPI, I8>::SMEM));
   if (dev < 64) done[dev] = true;
   return WX_OK;
 }
@@ -1054,7 +1077,8 @@ static int prepare_t(int bn, bool pair) {
 template <int BN, int EPI, bool I8>
 static int launch_t(const GemmPlan& p, cudaStream_t st) {
   if (p.pair) {
-    gemm2_bf16_kernel<EPI, I8><<<p.grid, kGemmThreads, Gemm2Cfg<EPI>::SMEM, st>>>(
+    gemm2_bf16_kernel<EPI, I8><<<p.grid, Gemm2Cfg<EPI, I8>::THREADS, Gemm2Cfg<EPI, I8>::SMEM,
+                                 st>>>(
         p.tmA, p.tmB, p.tmC, p.tmR, p.args);
     return check_launch(I8 ? "gemm_i8_pair" : "gemm_bf16_pair");
   }
