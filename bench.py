@@ -36,6 +36,9 @@ N_MELS, D, N_HEAD, N_LAYER, FFN, CTX = 128, 1280, 20, 32, 5120, 1500
 # on a 4-clip launch (profiles/attention_ncu_b4.md: 46.14 MB read, 0.28 MB
 # written); Q, K and V are read once, O stays in L2 at that size.
 ATTN_DRAM_BYTES_PER_CLIP = (46.173e6 + 0.453e6) / 4
+# ctx 512: 32 layers at T = 512 + the conv frontend over 1024 frames
+FLOP_PER_CLIP_512 = (32 * (8 * 512 * 1280 * 1280 + 4 * 512 * 1280 * 5120 + 4 * 512 * 512 * 1280)
+                     + 2 * 1024 * 384 * 1280 + 2 * 512 * 3840 * 1280)
 FLOP_PER_CLIP = (N_LAYER * (8 * CTX * D * D + 4 * CTX * D * FFN + 4 * CTX * CTX * D)
                  + 2 * (2 * CTX) * (3 * N_MELS) * D + 2 * CTX * (3 * D) * D)
 
@@ -301,6 +304,24 @@ def run_b200(args, rank, world, local_rank):
     t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     finite = bool(torch.isfinite(out).all().item())
 
+    # the ctx-512 variant of the same configuration: each clip's mel cut to its
+    # first 1024 frames (bench/run_raw_encoder.py:63-65), the same clips
+    mel512 = mel[:, :, :1024].contiguous()
+    out512 = torch.empty(B, 512, D, device="cuda")
+    for _ in range(args.warmup):
+        enc.forward(mel512, out=out512)
+    torch.cuda.synchronize()
+    barrier()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(st)
+    for _ in range(args.steps):
+        enc.forward(mel512, out=out512)
+    c1.record(st)
+    torch.cuda.synchronize()
+    barrier()
+    t_512 = max_over_ranks(c0.elapsed_time(c1) / 1e3)
+    del mel512, out512
+
     # ---- end to end through the public API, host buffers in and out
     mel_np, out_np = mel_host.numpy(), out_host.numpy()
     for _ in range(args.warmup):
@@ -384,6 +405,10 @@ def run_b200(args, rank, world, local_rank):
                              else (3 + 3 + 9 * N_LAYER + 1)) * args.steps,
             "roofline": roof, "kernels": kernels, "row_ops": row_ops, "clocks": clk,
             "batch1_latency": lat,
+            "ctx512": {"value": B * world * args.steps / t_512, "unit": UNIT,
+                       "ms_per_clip_per_gpu": t_512 / args.steps * 1e3 / B,
+                       "flop_per_clip": FLOP_PER_CLIP_512,
+                       "note": "the same clips with mel cut to 1024 frames (audio_ctx 512)"},
             "cpu_baseline": cpu, "output_finite": finite,
             "flop_per_clip": FLOP_PER_CLIP,
         }

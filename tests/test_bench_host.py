@@ -13,6 +13,8 @@ import encoder_ref as R
 def test_flop_per_clip_matches_the_work_table():
     # large-v3, ctx 1500: 32 x 70.50 GFLOP layers + 17.69 GFLOP conv = 2.2738 TFLOP
     assert bench.FLOP_PER_CLIP == pytest.approx(2.2738e12, rel=1e-4)
+    # ctx 512 (mel cut to 1024 frames): 0.6932 TFLOP
+    assert bench.FLOP_PER_CLIP_512 == pytest.approx(0.6932e12, rel=1e-4)
 
 
 def test_arm_config_names_the_workload():
