@@ -73,6 +73,30 @@ def test_reduced_audio_ctx(cuda):
     assert R.cosine(out, ref) >= 0.9999
 
 
+def test_graph_replays_follow_the_buffers(cuda):
+    """One captured graph per (batch, frames) serves any input and output
+    buffers: interleaved forwards with different buffers each read their own
+    mel and write their own output, equal to eager launches."""
+    W = R.make_weights("tiny", seed=6, n_layer=2)
+    enc = Encoder(W, n_layer=2, n_head=6, max_batch=2)
+    try:
+        mels = [torch.from_numpy(np.stack([R.make_mel(80, 300, seed=50 + 2 * i + j)
+                                           for j in range(2)])).cuda() for i in range(3)]
+        outs = [torch.full((2, 150, 384), float("nan"), device="cuda") for _ in range(4)]
+        enc.forward(mels[0], out=outs[0])
+        enc.forward(mels[1], out=outs[1])
+        enc.forward(mels[2], out=outs[2])
+        enc.forward(mels[0], out=outs[3])
+        torch.cuda.synchronize()
+        for i, m in ((0, 0), (1, 1), (2, 2), (3, 0)):
+            ref = enc.forward(mels[m], use_graph=False)
+            torch.cuda.synchronize()
+            assert torch.equal(outs[i], ref), i
+        assert not torch.equal(outs[0], outs[1])
+    finally:
+        enc.close()
+
+
 def test_device_forward_matches_host_forward(cuda):
     W = R.make_weights("tiny", seed=5)
     mel = R.make_mel(80, 3000, seed=6)

@@ -75,7 +75,9 @@ __global__ void permute_f32_kernel(const float* __restrict__ src, float* __restr
 // per 32 frames: the mel tile is staged in shared memory so reads run along
 // time and writes along the row.
 __global__ void __launch_bounds__(256) im2col_conv1_kernel(const float* __restrict__ mel,
-                                                           uint16_t* __restrict__ A, int C, int F) {
+                                                           uint16_t* __restrict__ A, int C, int F,
+                                                           const float* const* __restrict__ mel_ind) {
+  if (mel_ind) mel = *mel_ind;   // graph replays read the current input from here
   extern __shared__ float tile[];  // C x 34
   const int b = blockIdx.y;
   const int t0 = blockIdx.x * 32;
@@ -94,6 +96,18 @@ __global__ void __launch_bounds__(256) im2col_conv1_kernel(const float* __restri
     const int c = col / 3, j = col % 3;
     A[((int64_t)b * F + t) * K + col] = (uint16_t)bf16_bits<RND_RNE>(tile[c * 34 + r + j]);
   }
+}
+
+// The input and output pointers of one graph replay, written on the replay's
+// stream just before it: a captured forward reads mel and writes out through
+// them, so one graph per (batch, frames) serves every pair of buffers.
+struct IoPtrs {
+  const float* mel;
+  float* out;
+};
+__global__ void set_io_kernel(IoPtrs* io, const float* mel, float* out) {
+  io->mel = mel;
+  io->out = out;
 }
 
 // conv2 im2col with the j-major weight: A (batch*T, 3d) row t of clip b is
@@ -138,11 +152,8 @@ struct Plans {
 
 struct GraphKey {
   int64_t batch, frames;
-  const void* mel;
-  void* out;
-  cudaStream_t st;
   bool operator<(const GraphKey& o) const {
-    return std::tie(batch, frames, mel, out, st) < std::tie(o.batch, o.frames, o.mel, o.out, o.st);
+    return std::tie(batch, frames) < std::tie(o.batch, o.frames);
   }
 };
 
@@ -166,6 +177,7 @@ struct wx_encoder {
   uint16_t* f = nullptr;      // (B*T, ffn) bf16; also the im2col buffers
   float* mel_dev = nullptr;   // (B, n_mels, 2*n_ctx) staging for host input
   float* out_dev = nullptr;   // (B, n_ctx, d) staging for host output
+  wx::IoPtrs* io = nullptr;   // input / output pointers of the next graph replay
   float* stage = nullptr;     // fp32 upload staging for weights
   float* stage2 = nullptr;    // int8 mode: permuted fp32 weights
   int64_t stage_n = 0;
@@ -367,13 +379,14 @@ static int ln_quant(wx_encoder* e, const float* x, const float* g, const float* 
 
 // The launch sequence of one int8-mode forward pass.
 static int forward_launches_i8(wx_encoder* e, Plans* p, const float* mel, float* out, int64_t B,
-                               int64_t T, cudaStream_t st) {
+                               int64_t T, cudaStream_t st, const IoPtrs* io) {
   const int64_t M = B * T, F2 = 2 * T, d = e->d, ffn = e->ffn, K1 = 3 * (int64_t)e->n_mels;
   float* h32 = reinterpret_cast<float*>(e->f);   // fp32 LN output (f holds M*ffn bf16)
   {
     const size_t smem = (size_t)e->n_mels * 34 * 4;
     dim3 grid((unsigned)((F2 + 31) / 32), (unsigned)B);
-    im2col_conv1_kernel<<<grid, 256, smem, st>>>(mel, e->f, e->n_mels, (int)F2);
+    im2col_conv1_kernel<<<grid, 256, smem, st>>>(mel, e->f, e->n_mels, (int)F2,
+                                                  io ? &io->mel : nullptr);
     WX_TRY(check_launch("im2col_conv1"));
   }
   WX_TRY(launch_quantize_rows(e->f, WX_DTYPE_BF16, B * F2, K1, K1, nullptr, 0, e->fq, K1, e->sa, st));
@@ -402,19 +415,23 @@ static int forward_launches_i8(wx_encoder* e, Plans* p, const float* mel, float*
     WX_TRY(gemm_run(p->fc2[l], st));
   }
   WX_TRY(launch_layernorm_rows(e->x, WX_DTYPE_F32, e->lnp_g, e->lnp_b, out, WX_DTYPE_F32, M, d, d,
-                               d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st));
+                               d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st,
+                               io ? reinterpret_cast<void* const*>(&io->out) : nullptr));
   return WX_OK;
 }
 
 // The launch sequence of one forward pass.
+// io: when not NULL (graph capture), the first kernel reads mel and the last
+// writes out through it instead of the pointers given.
 static int forward_launches(wx_encoder* e, Plans* p, const float* mel, float* out, int64_t B,
-                            int64_t T, cudaStream_t st) {
-  if (e->quant) return forward_launches_i8(e, p, mel, out, B, T, st);
+                            int64_t T, cudaStream_t st, const IoPtrs* io) {
+  if (e->quant) return forward_launches_i8(e, p, mel, out, B, T, st, io);
   const int64_t M = B * T, F2 = 2 * T, d = e->d;
   {
     const size_t smem = (size_t)e->n_mels * 34 * 4;
     dim3 grid((unsigned)((F2 + 31) / 32), (unsigned)B);
-    im2col_conv1_kernel<<<grid, 256, smem, st>>>(mel, e->f, e->n_mels, (int)F2);
+    im2col_conv1_kernel<<<grid, 256, smem, st>>>(mel, e->f, e->n_mels, (int)F2,
+                                                  io ? &io->mel : nullptr);
     WX_TRY(check_launch("im2col_conv1"));
   }
   WX_TRY(gemm_run(p->conv1, st));
@@ -438,7 +455,8 @@ static int forward_launches(wx_encoder* e, Plans* p, const float* mel, float* ou
     WX_TRY(gemm_run(p->fc2[l], st));
   }
   WX_TRY(launch_layernorm_rows(e->x, WX_DTYPE_F32, e->lnp_g, e->lnp_b, out, WX_DTYPE_F32, M, d, d,
-                               d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st));
+                               d, 1e-5f, WX_LN_FP32, WX_ROUND_RNE, st,
+                               io ? reinterpret_cast<void* const*>(&io->out) : nullptr));
   return WX_OK;
 }
 
@@ -506,6 +524,7 @@ int wx_encoder_create(wx_encoder** out, int n_mels, int d_model, int n_head, int
   A((void**)&e->f, f_elems * 2);
   A((void**)&e->mel_dev, B * n_mels * 2 * T * 4);
   A((void**)&e->out_dev, M * d * 4);
+  A((void**)&e->io, sizeof(IoPtrs));
   e->stage_n = std::max((int64_t)ffn * d, std::max(3 * d * d, T * d));
   A((void**)&e->stage, e->stage_n * 4);
   if (s == WX_OK) {
@@ -687,16 +706,18 @@ int wx_encoder_forward(wx_encoder* e, const float* mel, float* out, int64_t batc
   Plans* p = nullptr;
   WX_TRY(build_plans(e, batch, T, &p));
   cudaStream_t st = as_stream(stream);
-  if (!use_graph) return forward_launches(e, p, mel, out, batch, T, st);
+  if (!use_graph) return forward_launches(e, p, mel, out, batch, T, st, nullptr);
   // Graphs are captured on a private stream fenced to the caller's stream by
-  // events, so the legacy default stream works too.
-  GraphKey key{batch, T, mel, out, st};
+  // events, so the legacy default stream works too. One graph per (batch,
+  // frames): its first and last kernels take the buffers from e->io, which
+  // set_io_kernel fills on the same stream right before each replay.
+  GraphKey key{batch, T};
   auto it = e->graphs.find(key);
   cudaGraphExec_t exec = nullptr;
   if (it == e->graphs.end()) {
     cudaGraph_t g = nullptr;
     WX_CUDA_TRY(cudaStreamBeginCapture(e->side, cudaStreamCaptureModeThreadLocal));
-    int s = forward_launches(e, p, mel, out, batch, T, e->side);
+    int s = forward_launches(e, p, mel, out, batch, T, e->side, e->io);
     cudaError_t ce = cudaStreamEndCapture(e->side, &g);
     if (s != WX_OK) {
       if (g) cudaGraphDestroy(g);
@@ -712,6 +733,8 @@ int wx_encoder_forward(wx_encoder* e, const float* mel, float* out, int64_t batc
   }
   WX_CUDA_TRY(cudaEventRecord(e->ev_in, st));
   WX_CUDA_TRY(cudaStreamWaitEvent(e->side, e->ev_in, 0));
+  set_io_kernel<<<1, 1, 0, e->side>>>(e->io, mel, out);
+  WX_TRY(check_launch("set_io"));
   WX_CUDA_TRY(cudaGraphLaunch(exec, e->side));
   WX_CUDA_TRY(cudaEventRecord(e->ev_out, e->side));
   WX_CUDA_TRY(cudaStreamWaitEvent(st, e->ev_out, 0));

@@ -81,9 +81,12 @@ int launch_gelu_poly4(const void* in, int in_dtype, void* out, int64_t rows, int
 int launch_softmax_rows(const void* in, void* out, int64_t rows, int64_t cols, int64_t valid,
                         int64_t ld_in, int64_t ld_out, float scale, int variant, int rounding,
                         cudaStream_t st);
+// out_ind (mode WX_LN_FP32 only): when not NULL the kernel reads its output
+// pointer from this device address (out is then ignored)
 int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, const float* beta,
                           void* out, int out_dtype, int64_t rows, int64_t cols, int64_t ld_in,
-                          int64_t ld_out, float eps, int mode, int rounding, cudaStream_t st);
+                          int64_t ld_out, float eps, int mode, int rounding, cudaStream_t st,
+                          void* const* out_ind = nullptr);
 
 int launch_layernorm_quant_rows(const float* in, const float* gamma, const float* beta, int8_t* q,
                                 float* scale, int64_t rows, int64_t cols, int64_t ld_in,

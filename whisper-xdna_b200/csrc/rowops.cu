@@ -693,11 +693,14 @@ __global__ void __launch_bounds__(256) layernorm_aie_reg_kernel(
 
 // fp32 two-pass LayerNorm, one warp per row; the row is kept in registers as
 // NV float4 per lane (NV * 128 >= width; NV = 0: any width, re-read from L2).
+// out_ind: when not NULL, the output pointer is read from device memory there
+// (so that a captured graph can write to a different buffer on each replay).
 template <bool IN_BF16, bool OUT_BF16, int NV>
 __global__ void __launch_bounds__(256) layernorm_fp32_kernel(
     const void* __restrict__ in, const float* __restrict__ gamma,
     const float* __restrict__ beta, void* __restrict__ out, int64_t rows, int w, int64_t ld_in,
-    int64_t ld_out, float eps) {
+    int64_t ld_out, float eps, void* const* __restrict__ out_ind) {
+  if (out_ind) out = *out_ind;
   constexpr int NR = NV > 0 ? NV : 1;
   const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
   auto load4 = [&](int64_t row, int c) -> float4 {
@@ -849,10 +852,10 @@ __global__ void __launch_bounds__(256) layernorm_quant_kernel(
 template <bool IB, bool OB>
 static void launch_ln_fp32(int grid, cudaStream_t st, const void* in, const float* gamma,
                            const float* beta, void* out, int64_t rows, int w, int64_t ld_in,
-                           int64_t ld_out, float eps) {
+                           int64_t ld_out, float eps, void* const* out_ind) {
   const int nv = (w + 127) / 128;
 #define WX_LN_CASE(N) \
-  layernorm_fp32_kernel<IB, OB, N><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, w, ld_in, ld_out, eps)
+  layernorm_fp32_kernel<IB, OB, N><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, w, ld_in, ld_out, eps, out_ind)
   if (nv <= 3) WX_LN_CASE(3);
   else if (nv <= 4) WX_LN_CASE(4);
   else if (nv <= 6) WX_LN_CASE(6);
@@ -988,8 +991,11 @@ int launch_softmax_rows(const void* in, void* out, int64_t rows, int64_t cols, i
 
 int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, const float* beta,
                           void* out, int out_dtype, int64_t rows, int64_t cols, int64_t ld_in,
-                          int64_t ld_out, float eps, int mode, int rounding, cudaStream_t st) {
+                          int64_t ld_out, float eps, int mode, int rounding, cudaStream_t st,
+                          void* const* out_ind) {
   if (rows < 0 || cols < 0) return fail(WX_ERR_INVALID, "layernorm: negative shape");
+  if (out_ind && mode != WX_LN_FP32)
+    return fail(WX_ERR_INVALID, "layernorm: an indirect output needs mode WX_LN_FP32");
   if (rows == 0 || cols == 0) return WX_OK;
   if (!in || !out) return fail(WX_ERR_INVALID, "layernorm: NULL pointer");
   if (ld_in < cols || ld_out < cols) return fail(WX_ERR_INVALID, "layernorm: row stride < cols");
@@ -1055,10 +1061,14 @@ int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, cons
   const int grid = grid_for(rows, 8, 8);
   const bool ib = in_dtype == WX_DTYPE_BF16, ob = out_dtype == WX_DTYPE_BF16;
   const int w = (int)cols;
-  if (ib && ob) launch_ln_fp32<true, true>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps);
-  else if (ib) launch_ln_fp32<true, false>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps);
-  else if (ob) launch_ln_fp32<false, true>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps);
-  else launch_ln_fp32<false, false>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps);
+  if (ib && ob) launch_ln_fp32<true, true>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps,
+                                             out_ind);
+  else if (ib) launch_ln_fp32<true, false>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps,
+                                             out_ind);
+  else if (ob) launch_ln_fp32<false, true>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps,
+                                             out_ind);
+  else launch_ln_fp32<false, false>(grid, st, in, gamma, beta, out, rows, w, ld_in, ld_out, eps,
+                                             out_ind);
   return check_launch("layernorm_fp32");
 }
 
@@ -1116,7 +1126,7 @@ int wx_layernorm_rows(const void* in, int in_dtype, const float* gamma, const fl
                       void* out, int out_dtype, int64_t rows, int64_t cols, int64_t ld_in,
                       int64_t ld_out, float eps, int mode, int rounding, void* stream) {
   return wx::launch_layernorm_rows(in, in_dtype, gamma, beta, out, out_dtype, rows, cols, ld_in,
-                                   ld_out, eps, mode, rounding, wx::as_stream(stream));
+                                   ld_out, eps, mode, rounding, wx::as_stream(stream), nullptr);
 }
 
 int wx_softmax_exp_table(int rounding, uint16_t* out16, float* out32, int64_t n) {
