@@ -144,6 +144,11 @@ def test_gemm_i8_epilogues(cuda, M, N, K):
     acc = ops.gemm_i8(qa, qw, sa, sw, bias=bias)
     x = torch.randn(M, N, generator=g).cuda()
     want = (acc + x).cpu().numpy()
+    # residual read by the epilogue (separate output) and added in place
+    # (the CTA-pair kernel reduce-adds into C): the same bits
+    y = torch.empty_like(x)
+    ops.gemm_i8(qa, qw, sa, sw, bias=bias, residual=x, out=y, epilogue=L.WX_EPI_F32_RESID)
+    assert np.array_equal(y.cpu().numpy(), want)
     ops.gemm_i8(qa, qw, sa, sw, bias=bias, residual=x, out=x, epilogue=L.WX_EPI_F32_RESID)
     assert np.array_equal(x.cpu().numpy(), want)
     b16 = ops.gemm_i8(qa, qw, sa, sw, bias=bias, epilogue=L.WX_EPI_BF16)

@@ -276,8 +276,10 @@ __device__ __forceinline__ uint32_t epi_chunk_to_smem(const GemmArgs& a, uint32_
     for (int j = 0; j < 8; j++) {
       float4* p = reinterpret_cast<float4*>(rowp + ((j ^ sw) << 4));
       if constexpr (EPI == WX_EPI_F32_RESID) {
-        const float4 t = *p;
-        v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+        if (!a.resid_inplace) {
+          const float4 t = *p;
+          v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+        }
       }
       *p = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
@@ -761,10 +763,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Cfg<EPI, I8>::T
       lc++;
       lk++;
     };
-    if constexpr (EPI == WX_EPI_F32_RESID) {
-      if (lane == 0)
-        for (int i = 0; i < NB; i++) load_next();
-    }
+    // residual in place (C == R): the epilogue writes acc + bias and a TMA
+    // reduce-add folds it into C, so no residual is loaded
+    const bool resid_ld = EPI == WX_EPI_F32_RESID && !a.resid_inplace;
+    if (resid_ld && lane == 0)
+      for (int i = 0; i < NB; i++) load_next();
     int acc = 0;
     uint32_t acc_phase = 0, k = 0;
     for (int tile = pair; ok && tile < a.num_tiles; tile += npairs) {
@@ -781,7 +784,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Cfg<EPI, I8>::T
       uint32_t mx = 0;
       for (int c = 0; c < nc; c++, k++) {
         uint8_t* buf = ebuf + (k % NB) * kEpiBufBytes;
-        if constexpr (EPI == WX_EPI_F32_RESID) {
+        if (resid_ld) {
           ok = __all_sync(0xffffffffu, mbar_wait(&rf[k % NB], (k / NB) & 1, a.err));
           if (!ok) break;
         } else {
@@ -794,9 +797,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Cfg<EPI, I8>::T
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf, c0 + c * kCols, r0);
+          if (EPI == WX_EPI_F32_RESID && a.resid_inplace)
+            tma_reduce_add_2d(&tmC, buf, c0 + c * kCols, r0);
+          else
+            tma_store_2d(&tmC, buf, c0 + c * kCols, r0);
           bulk_commit_group();
-          if constexpr (EPI == WX_EPI_F32_RESID) {
+          if (resid_ld) {
             bulk_wait_group_read<0>();   // the store has read buf: refill it
             load_next();
           }
@@ -961,6 +967,9 @@ static int gemm_plan_impl(GemmPlan* p, const void* A, const void* B, const float
   g.sa = sa;
   g.sw = sw;
   g.rowmax = rowmax;
+  // In-place residual by TMA reduce-add: int8 plans only. Measured on B200, it
+  // speeds the int8 fc2 GEMM by 2.6% and slows the bf16 out-proj GEMM by 2.3%.
+  g.resid_inplace = (epi == WX_EPI_F32_RESID && i8 && pair && R == C && ldr == ldc) ? 1 : 0;
   p->bn = bn;
   p->epi = epi;
   p->pair = pair;
@@ -1034,6 +1043,7 @@ int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, cons
   g.sa = nullptr;
   g.sw = nullptr;
   g.rowmax = nullptr;
+  g.resid_inplace = 0;
   p->bn = bn;
   p->epi = epi;
   p->pair = pair;

@@ -21,6 +21,7 @@ struct GemmArgs {
   const float* sa;   // per-row (token) scales of A
   const float* sw;   // per-column (channel) scales of B
   float* rowmax;     // bf16 outputs: max |value| of each row, atomically (or NULL)
+  int resid_inplace; // WX_EPI_F32_RESID with C == R: the 2-SM kernel adds into C by TMA
 };
 
 // Epilogues used only inside the library (the conv2 step of the encoder):
