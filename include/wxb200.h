@@ -255,15 +255,32 @@ int wx_encoder_set_quant(wx_encoder* enc, int mode);
  * out (batch, n_frames / 2, d_model) fp32. n_frames even, n_frames / 2 <= n_ctx
  * (a shortened mel is a reduced audio_ctx, bench/run_raw_encoder.py:63-65).
  * When use_graph != 0 the launch sequence is captured once per (batch,
- * n_frames, mel, out, stream) and replayed as a CUDA graph. */
+ * n_frames) and replayed as a CUDA graph on any buffers and stream. */
 int wx_encoder_forward(wx_encoder* enc, const float* mel, float* out, int64_t batch,
                        int64_t n_frames, int use_graph, void* stream);
 
 /* Forward on HOST buffers (pinned memory gives asynchronous copies): copies
  * mel in, runs wx_encoder_forward, copies the result out, and synchronizes
- * the stream before returning. */
+ * the stream before returning. Batches submitted by wx_encoder_submit_host
+ * are waited for first. */
 int wx_encoder_forward_host(wx_encoder* enc, const float* mel_host, float* out_host,
                             int64_t batch, int64_t n_frames, int use_graph, void* stream);
+
+/* Pipelined forward on HOST buffers, for a stream of batches (the server's
+ * windows, serve/npu_stt_server.py:421-431, or the throughput loop of
+ * bench/run_raw_encoder.py, each of which calls encoder(),
+ * src/npu_whisper_encoder.py:436-541, once per input). Enqueues the copy-in,
+ * the forward and the copy-out of one batch and returns; one batch's copies
+ * overlap the neighbouring batches' compute. Two batches are in flight at
+ * most: a call waits until the batch submitted two calls earlier is in its
+ * host buffer. mel_host and out_host must stay valid, and unmodified, until
+ * wx_encoder_wait_host returns (pinned memory for the overlap). One host
+ * thread per handle. */
+int wx_encoder_submit_host(wx_encoder* enc, const float* mel_host, float* out_host,
+                           int64_t batch, int64_t n_frames, int use_graph);
+
+/* Blocks until every submitted batch's features are in its host buffer. */
+int wx_encoder_wait_host(wx_encoder* enc);
 
 /* Device memory the encoder holds (weights + workspace), in bytes. */
 int64_t wx_encoder_device_bytes(const wx_encoder* enc);

@@ -109,3 +109,6 @@ def test_invalid_arguments_rejected_before_any_launch(wxlib):
     assert wxlib.wx_gemm_i8(a, a, a, a, nul, nul, a, 32, 32, 32, 32, 32, 32, 0, 9, nul,
                             nul) == L.WX_ERR_INVALID
     assert wxlib.wx_encoder_set_quant(nul, L.WX_QUANT_INT8_PERCHAN) == L.WX_ERR_INVALID
+    # the pipelined host entry points check the handle before any CUDA call
+    assert wxlib.wx_encoder_submit_host(nul, nul, nul, 1, 400, 1) == L.WX_ERR_INVALID
+    assert wxlib.wx_encoder_wait_host(nul) == L.WX_ERR_INVALID

@@ -132,6 +132,44 @@ def test_pipelined_host_forward_matches_device_forward(cuda, batch):
     assert L.device_error() == 0
 
 
+def test_submitted_batches_match_device_forward(cuda):
+    """submit_host / wait_host: a stream of batches of different sizes and
+    frame counts, two in flight, pinned and pageable buffers, with a
+    synchronous forward_host in between; each batch's features equal the
+    device forward of that batch."""
+    W = R.make_weights("tiny", seed=5, n_layer=2)
+    enc = Encoder(W, n_layer=2, max_batch=4)
+    try:
+        cases = [(4, 400), (3, 400), (4, 300), (1, 400), (4, 400), (2, 200)]
+        mels = [np.stack([R.make_mel(80, F, seed=70 + 10 * k + i) for i in range(B)])
+                for k, (B, F) in enumerate(cases)]
+        pinned = [torch.from_numpy(m).pin_memory() for m in mels]
+        outs = [torch.full((B, F // 2, 384), float("nan")).pin_memory() for B, F in cases]
+        pageable_out = np.full((3, 200, 384), np.nan, dtype=np.float32)
+        enc.submit_host(pinned[0].numpy(), outs[0].numpy())
+        enc.submit_host(mels[1], pageable_out)                 # pageable: the copies block
+        enc.submit_host(pinned[2].numpy(), outs[2].numpy())    # waits for batch 0's slot
+        sync = enc.forward_host(mels[3])                       # drains the queue first
+        enc.submit_host(pinned[4].numpy(), outs[4].numpy())
+        enc.submit_host(pinned[5].numpy(), outs[5].numpy())
+        enc.wait_host()
+        enc.wait_host()                                        # nothing in flight: returns
+        got = [outs[0].numpy(), pageable_out, outs[2].numpy(), sync, outs[4].numpy(),
+               outs[5].numpy()]
+        for k, m in enumerate(mels):
+            ref = enc.forward(torch.from_numpy(m).cuda())
+            torch.cuda.synchronize()
+            assert np.array_equal(got[k], ref.cpu().numpy()), k
+        with pytest.raises(ValueError):
+            enc.submit_host(mels[0], np.empty((4, 199, 384), dtype=np.float32))
+        with pytest.raises(ValueError):
+            enc.submit_host(np.stack([R.make_mel(80, 400, seed=1)] * 5),
+                            np.empty((5, 200, 384), dtype=np.float32))   # over max_batch
+    finally:
+        enc.close()
+    assert L.device_error() == 0
+
+
 def test_dropin_encoder_signature(cuda):
     """encoder(W, mel, RT.matmul, RT.matmul, ..., attn_fn=RT.attn_chain,
     mlp_fn=RT.mlp, fold_bias=True) -- the server's call (serve/npu_stt_server.py:340-342)."""

@@ -202,6 +202,13 @@ struct wx_encoder {
   cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
   cudaEvent_t ev_start = nullptr, ev_end = nullptr;
   cudaEvent_t ev_h2d[kHostChunks] = {}, ev_done[kHostChunks] = {};
+  // the pipelined host entry point (submit / wait): two staging slots, slot 0
+  // is mel_dev / out_dev, slot 1 is allocated on first use
+  float* mel_dev1 = nullptr;
+  float* out_dev1 = nullptr;
+  cudaEvent_t ev_q_in[2] = {}, ev_q_comp[2] = {}, ev_q_out[2] = {};
+  bool q_busy[2] = {false, false};
+  int q_next = 0;
   std::mutex mu;
 };
 
@@ -539,6 +546,10 @@ int wx_encoder_create(wx_encoder** out, int n_mels, int d_model, int n_head, int
     for (int k = 0; good && k < wx_encoder::kHostChunks; k++)
       good = cudaEventCreateWithFlags(&e->ev_h2d[k], cudaEventDisableTiming) == cudaSuccess &&
              cudaEventCreateWithFlags(&e->ev_done[k], cudaEventDisableTiming) == cudaSuccess;
+    for (int k = 0; good && k < 2; k++)
+      good = cudaEventCreateWithFlags(&e->ev_q_in[k], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&e->ev_q_comp[k], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&e->ev_q_out[k], cudaEventDisableTiming) == cudaSuccess;
     if (!good) s = fail(WX_ERR_CUDA, "encoder_create: stream/event creation failed");
   }
   if (s != WX_OK) {
@@ -551,6 +562,9 @@ int wx_encoder_create(wx_encoder** out, int n_mels, int d_model, int n_head, int
 
 int wx_encoder_destroy(wx_encoder* e) {
   if (!e) return WX_OK;
+  // submitted batches finish writing their host buffers first
+  for (int k = 0; k < 2; k++)
+    if (e->q_busy[k]) cudaEventSynchronize(e->ev_q_out[k]);
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : e->plans) delete kv.second;
   for (void* p : e->allocs) cudaFree(p);
@@ -565,6 +579,9 @@ int wx_encoder_destroy(wx_encoder* e) {
     if (e->ev_h2d[k]) cudaEventDestroy(e->ev_h2d[k]);
     if (e->ev_done[k]) cudaEventDestroy(e->ev_done[k]);
   }
+  for (int k = 0; k < 2; k++)
+    for (cudaEvent_t x : {e->ev_q_in[k], e->ev_q_comp[k], e->ev_q_out[k]})
+      if (x) cudaEventDestroy(x);
   delete e;
   return WX_OK;
 }
@@ -748,6 +765,7 @@ int wx_encoder_forward_host(wx_encoder* e, const float* mel_host, float* out_hos
   if (batch <= 0 || batch > e->max_batch || n_frames <= 0 || n_frames % 2 ||
       n_frames / 2 > e->n_ctx)
     return fail(WX_ERR_INVALID, "encoder_forward_host: bad batch or n_frames");
+  WX_TRY(wx_encoder_wait_host(e));   // submitted batches share slot 0's staging
   cudaStream_t st = as_stream(stream);
   const int64_t T = n_frames / 2;
   const size_t in_clip = (size_t)e->n_mels * n_frames, out_clip = (size_t)T * e->d;
@@ -780,6 +798,57 @@ int wx_encoder_forward_host(wx_encoder* e, const float* mel_host, float* out_hos
   WX_CUDA_TRY(cudaEventRecord(e->ev_end, e->s_out));
   WX_CUDA_TRY(cudaStreamWaitEvent(st, e->ev_end, 0));
   WX_CUDA_TRY(cudaStreamSynchronize(st));
+  return WX_OK;
+}
+
+int wx_encoder_submit_host(wx_encoder* e, const float* mel_host, float* out_host, int64_t batch,
+                           int64_t n_frames, int use_graph) {
+  if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  if (!mel_host || !out_host) return fail(WX_ERR_INVALID, "encoder_submit_host: NULL buffer");
+  if (batch <= 0 || batch > e->max_batch || n_frames <= 0 || n_frames % 2 ||
+      n_frames / 2 > e->n_ctx)
+    return fail(WX_ERR_INVALID, "encoder_submit_host: bad batch or n_frames");
+  const int k = e->q_next;
+  if (k == 1 && !e->mel_dev1) {
+    WX_TRY(dalloc(e, (void**)&e->mel_dev1, (int64_t)e->max_batch * e->n_mels * 2 * e->n_ctx * 4));
+    WX_TRY(dalloc(e, (void**)&e->out_dev1, (int64_t)e->max_batch * e->n_ctx * e->d * 4));
+  }
+  // at most two batches in flight: the one submitted two calls ago has
+  // finished with its host buffers before this one takes its slot
+  if (e->q_busy[k]) {
+    WX_CUDA_TRY(cudaEventSynchronize(e->ev_q_out[k]));
+    e->q_busy[k] = false;
+  }
+  const int64_t T = n_frames / 2;
+  const size_t in_bytes = (size_t)batch * e->n_mels * n_frames * 4;
+  const size_t out_bytes = (size_t)batch * T * e->d * 4;
+  float* md = k ? e->mel_dev1 : e->mel_dev;
+  float* od = k ? e->out_dev1 : e->out_dev;
+  // The copy-in waits for the compute that last read this slot; the compute
+  // waits for its copy-in and for the copy-out that last read this slot's
+  // features; computes follow one another on s_comp.
+  WX_CUDA_TRY(cudaStreamWaitEvent(e->s_in, e->ev_q_comp[k], 0));
+  WX_CUDA_TRY(cudaMemcpyAsync(md, mel_host, in_bytes, cudaMemcpyHostToDevice, e->s_in));
+  WX_CUDA_TRY(cudaEventRecord(e->ev_q_in[k], e->s_in));
+  WX_CUDA_TRY(cudaStreamWaitEvent(e->s_comp, e->ev_q_in[k], 0));
+  WX_CUDA_TRY(cudaStreamWaitEvent(e->s_comp, e->ev_q_out[k], 0));
+  WX_TRY(wx_encoder_forward(e, md, od, batch, n_frames, use_graph, e->s_comp));
+  WX_CUDA_TRY(cudaEventRecord(e->ev_q_comp[k], e->s_comp));
+  WX_CUDA_TRY(cudaStreamWaitEvent(e->s_out, e->ev_q_comp[k], 0));
+  WX_CUDA_TRY(cudaMemcpyAsync(out_host, od, out_bytes, cudaMemcpyDeviceToHost, e->s_out));
+  WX_CUDA_TRY(cudaEventRecord(e->ev_q_out[k], e->s_out));
+  e->q_busy[k] = true;
+  e->q_next = k ^ 1;
+  return WX_OK;
+}
+
+int wx_encoder_wait_host(wx_encoder* e) {
+  if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  for (int k = 0; k < 2; k++) {
+    if (!e->q_busy[k]) continue;
+    e->q_busy[k] = false;
+    WX_CUDA_TRY(cudaEventSynchronize(e->ev_q_out[k]));
+  }
   return WX_OK;
 }
 

@@ -62,6 +62,8 @@ SIGNATURES = {
     "wx_encoder_set_quant": (_i, [_p, _i]),
     "wx_encoder_forward": (_i, [_p, _p, _p, _i64, _i64, _i, _p]),
     "wx_encoder_forward_host": (_i, [_p, _p, _p, _i64, _i64, _i, _p]),
+    "wx_encoder_submit_host": (_i, [_p, _p, _p, _i64, _i64, _i]),
+    "wx_encoder_wait_host": (_i, [_p]),
     "wx_encoder_device_bytes": (_i64, [_p]),
     "wx_log_mel": (_i, [_p, _i64, _i64, _i64, _i, _p, _p]),
     "wx_selftest_wait_timeout": (_i, [_c.c_uint64, _p]),

@@ -154,10 +154,38 @@ class Encoder:
                                                 1 if use_graph else 0, st))
         return out[0] if squeeze else out
 
+    def submit_host(self, mel, out):
+        """Pipelined forward_host for a stream of batches: enqueue the copy-in,
+        forward and copy-out of one batch and return at once, so one batch's
+        copies overlap its neighbours' compute (wx_encoder_submit_host). `mel`
+        (batch, n_mels, n_frames) and `out` (batch, n_frames/2, d) are C-contiguous
+        fp32 numpy arrays, pinned for the overlap (e.g. views of pinned torch
+        tensors); both must stay untouched until wait_host(). Two batches are in
+        flight at most: a call waits for the batch submitted two calls earlier."""
+        if not (isinstance(mel, np.ndarray) and isinstance(out, np.ndarray)):
+            raise TypeError("submit_host takes numpy arrays (the copies read and write them later)")
+        if (mel.dtype != np.float32 or out.dtype != np.float32 or mel.ndim != 3 or out.ndim != 3
+                or not mel.flags.c_contiguous or not out.flags.c_contiguous):
+            raise ValueError("submit_host: mel and out must be C-contiguous 3-D fp32 arrays")
+        B, C, F = mel.shape
+        if C != self.n_mels:
+            raise ValueError(f"mel has {C} bins, the weights expect {self.n_mels}")
+        if out.shape != (B, F // 2, self.d):
+            raise ValueError(f"out must be {(B, F // 2, self.d)}, got {out.shape}")
+        L.check(L.lib().wx_encoder_submit_host(self._h, mel.ctypes.data_as(ctypes.c_void_p),
+                                               out.ctypes.data_as(ctypes.c_void_p), B, F, 1))
+        self._inflight = (getattr(self, "_inflight", []) + [(mel, out)])[-2:]
+
+    def wait_host(self):
+        """Block until every submitted batch's features are in its `out`."""
+        L.check(L.lib().wx_encoder_wait_host(self._h))
+        self._inflight = []
+
     def close(self):
         if getattr(self, "_h", None):
             L.lib().wx_encoder_destroy(self._h)
             self._h = None
+            self._inflight = []
 
     def __del__(self):
         try:
