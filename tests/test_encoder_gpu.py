@@ -132,6 +132,37 @@ def test_pipelined_host_forward_matches_device_forward(cuda, batch):
     assert L.device_error() == 0
 
 
+def test_forwards_on_different_streams_are_ordered(cuda):
+    """The workspace is shared: a submitted host batch, a graph forward on one
+    stream and an eager forward on another, issued without synchronising,
+    each equal the same forward run alone."""
+    W = R.make_weights("tiny", seed=8, n_layer=2)
+    enc = Encoder(W, n_layer=2, max_batch=2)
+    try:
+        mels = [np.stack([R.make_mel(80, 400, seed=90 + 2 * i + j) for j in range(2)])
+                for i in range(3)]
+        alone = []
+        for m in mels:
+            alone.append(enc.forward(torch.from_numpy(m).cuda(), use_graph=False).cpu().numpy())
+        dev = [torch.from_numpy(m).cuda() for m in mels[1:]]
+        torch.cuda.synchronize()
+        pinned = torch.from_numpy(mels[0]).pin_memory()
+        out0 = torch.full((2, 200, 384), float("nan")).pin_memory()
+        enc.submit_host(pinned.numpy(), out0.numpy())
+        side = torch.cuda.Stream()
+        g = enc.forward(dev[0])                                  # graph, current stream
+        with torch.cuda.stream(side):
+            e = enc.forward(dev[1], use_graph=False)             # eager, another stream
+        enc.wait_host()
+        torch.cuda.synchronize()
+        assert np.array_equal(out0.numpy(), alone[0])
+        assert np.array_equal(g.cpu().numpy(), alone[1])
+        assert np.array_equal(e.cpu().numpy(), alone[2])
+    finally:
+        enc.close()
+    assert L.device_error() == 0
+
+
 def test_submitted_batches_match_device_forward(cuda):
     """submit_host / wait_host: a stream of batches of different sizes and
     frame counts, two in flight, pinned and pageable buffers, with a

@@ -723,7 +723,14 @@ int wx_encoder_forward(wx_encoder* e, const float* mel, float* out, int64_t batc
   Plans* p = nullptr;
   WX_TRY(build_plans(e, batch, T, &p));
   cudaStream_t st = as_stream(stream);
-  if (!use_graph) return forward_launches(e, p, mel, out, batch, T, st, nullptr);
+  // Forwards share the workspace, so each one waits for the previous one
+  // (ev_out marks the last forward's end) whatever stream either ran on.
+  if (!use_graph) {
+    WX_CUDA_TRY(cudaStreamWaitEvent(st, e->ev_out, 0));
+    WX_TRY(forward_launches(e, p, mel, out, batch, T, st, nullptr));
+    WX_CUDA_TRY(cudaEventRecord(e->ev_out, st));
+    return WX_OK;
+  }
   // Graphs are captured on a private stream fenced to the caller's stream by
   // events, so the legacy default stream works too. One graph per (batch,
   // frames): its first and last kernels take the buffers from e->io, which
@@ -750,6 +757,7 @@ int wx_encoder_forward(wx_encoder* e, const float* mel, float* out, int64_t batc
   }
   WX_CUDA_TRY(cudaEventRecord(e->ev_in, st));
   WX_CUDA_TRY(cudaStreamWaitEvent(e->side, e->ev_in, 0));
+  WX_CUDA_TRY(cudaStreamWaitEvent(e->side, e->ev_out, 0));
   set_io_kernel<<<1, 1, 0, e->side>>>(e->io, mel, out);
   WX_TRY(check_launch("set_io"));
   WX_CUDA_TRY(cudaGraphLaunch(exec, e->side));
