@@ -216,8 +216,11 @@ namespace wx {
 
 static int dalloc(wx_encoder* e, void** p, int64_t bytes) {
   cudaError_t r = cudaMalloc(p, (size_t)bytes);
-  if (r != cudaSuccess)
+  if (r != cudaSuccess) {
+    *p = nullptr;
+    cudaGetLastError();   // an allocation failure is not a launch error of a later kernel
     return fail(WX_ERR_NOMEM, "cudaMalloc(%lld) failed: %s", (long long)bytes, cudaGetErrorString(r));
+  }
   e->allocs.push_back(*p);
   e->bytes += bytes;
   return WX_OK;
@@ -817,10 +820,10 @@ int wx_encoder_submit_host(wx_encoder* e, const float* mel_host, float* out_host
       n_frames / 2 > e->n_ctx)
     return fail(WX_ERR_INVALID, "encoder_submit_host: bad batch or n_frames");
   const int k = e->q_next;
-  if (k == 1 && !e->mel_dev1) {
+  if (k == 1 && !e->mel_dev1)
     WX_TRY(dalloc(e, (void**)&e->mel_dev1, (int64_t)e->max_batch * e->n_mels * 2 * e->n_ctx * 4));
+  if (k == 1 && !e->out_dev1)
     WX_TRY(dalloc(e, (void**)&e->out_dev1, (int64_t)e->max_batch * e->n_ctx * e->d * 4));
-  }
   // at most two batches in flight: the one submitted two calls ago has
   // finished with its host buffers before this one takes its slot
   if (e->q_busy[k]) {
