@@ -50,6 +50,37 @@ def test_attention_matches_fp32(cuda, B, T, H):
     check(got, ref_attention(qkv, B, T, H, 1 / 8), qkv[:, 2 * d:])
 
 
+@pytest.mark.parametrize("B,T,H", [(64, 512, 20), (40, 300, 1), (149, 200, 1), (300, 150, 1),
+                                   (4, 1152, 20), (4, 1153, 20)])
+def test_attention_persistent_many_items(cuda, B, T, H):
+    """Items of at most 12 key blocks (T <= 1152) run on the persistent kernel,
+    one CTA per SM walking several (tile pair, head, clip) items; 1153 is the
+    first length on the per-item kernel. Checked per clip against fp32, and
+    equal bit for bit to the same clips run one at a time (one clip has fewer
+    items than SMs, so there every CTA takes a single item): carrying the
+    pipeline from one item to the next must not change any result."""
+    qkv = qkv_rand(B, T, H, 4000 + B + T + H)
+    d = H * 64
+    got = A.attn_heads(qkv, H, scale=1 / 8, n_batch=B)
+    for b in range(0, B, max(1, B // 4)):
+        rows = slice(b * T, (b + 1) * T)
+        check(got[rows], ref_attention(qkv[rows], 1, T, H, 1 / 8), qkv[rows, 2 * d:])
+    per_clip = torch.cat([A.attn_heads(qkv[b * T:(b + 1) * T], H, scale=1 / 8) for b in range(B)])
+    assert torch.equal(got, per_clip)
+
+
+def test_attention_persistent_zero_keys_gives_column_mean(cuda):
+    """The K = 0 known answer on the persistent kernel (ctx 512, 8 clips)."""
+    B, T, H = 8, 512, 20
+    qkv = qkv_rand(B, T, H, 17)
+    d = H * 64
+    qkv[:, d:2 * d] = 0
+    got = A.attn_heads(qkv, H, n_batch=B).float().view(B, T, d)
+    v = qkv[:, 2 * d:].float().view(B, T, d)
+    mean = v.mean(dim=1, keepdim=True).expand_as(got)
+    assert (got - mean).abs().max().item() < 1e-2
+
+
 def test_attention_batch16_large(cuda):
     """BASELINE attention config: T=1500, 20 heads x 64, batch 16."""
     B, T, H = 16, 1500, 20

@@ -59,6 +59,7 @@ void gemm_set_pos(GemmPlan* p, const float* pos, int64_t ldp, int pos_T);
 
 struct AttnArgs {
   int T, H, num_q_tiles;
+  int n_items;  // num_q_tiles * H * B work items (query tile pair, head, clip)
   void* O;
   int64_t ldo;
   float scale_log2;
@@ -69,6 +70,8 @@ struct AttnPlan {
   CUtensorMap tmQ, tmK, tmV;
   AttnArgs args;
   int B;
+  int grid;      // persistent kernel: min(items, SMs) CTAs
+  bool persist;  // run the persistent kernel (short items)
 };
 
 int attn_plan(AttnPlan* p, const void* q, const void* k, const void* v, void* o, int64_t B,
