@@ -25,17 +25,19 @@ from . import ops
 D, H, FFN, T = 1280, 20, 5120, 1500
 
 
-def setup(kernel, batch, dev="cuda"):
-    """Return (fn, flop_per_launch, bytes_per_launch) for one kernel."""
+def setup(kernel, batch, dev="cuda", ctx=T):
+    """Return (fn, flop_per_launch, bytes_per_launch) for one kernel; ctx is
+    the frame count of the attention kernel's clips (the encoder's T)."""
     g = torch.Generator(device=dev).manual_seed(0)
     M = batch * T
     rn = lambda *s, sc=1.0: (torch.randn(*s, device=dev, generator=g) * sc)
     if kernel == "attention":
-        qkv = rn(M, 3 * D).to(torch.bfloat16)
-        o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+        Ma = batch * ctx
+        qkv = rn(Ma, 3 * D).to(torch.bfloat16)
+        o = torch.empty(Ma, D, device=dev, dtype=torch.bfloat16)
         fn = lambda: ops.attention(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], batch, H, 0.125,
                                    out=o)
-        return fn, 4.0 * batch * T * T * D, 4.0 * M * D * 2
+        return fn, 4.0 * batch * ctx * ctx * D, 4.0 * Ma * D * 2
     if kernel in ("fc1", "fc2", "qkv", "outproj"):
         K, N = {"fc1": (D, FFN), "fc2": (FFN, D), "qkv": (D, 3 * D), "outproj": (D, D)}[kernel]
         A = rn(M, K).to(torch.bfloat16)
@@ -120,8 +122,8 @@ def setup(kernel, batch, dev="cuda"):
     raise ValueError(f"unknown kernel {kernel!r}")
 
 
-def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False):
-    fn, flop, byt = setup(kernel, batch)
+def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T):
+    fn, flop, byt = setup(kernel, batch, ctx=ctx)
     # 1 GiB: its fill (~160 us) outlasts the host-side cost of one launch
     junk = torch.empty(1024 * 1024 * 1024 // 4, device="cuda") if flush else None
     st = torch.cuda.current_stream()
@@ -154,6 +156,8 @@ def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False):
     t = total / iters
     res = {"kernel": kernel, "batch": batch, "s": t, "flop": flop, "bytes": byt,
            "flush_l2": bool(flush)}
+    if kernel == "attention":
+        res["ctx"] = ctx
     if flop:
         res["tflops"] = flop / t / 1e12
     res["gbs"] = byt / t / 1e9
@@ -167,8 +171,10 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--flush", action="store_true")
+    ap.add_argument("--ctx", type=int, default=T,
+                    help="attention only: frames per clip (T <= 1152 runs the persistent kernel)")
     a = ap.parse_args()
-    res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush)
+    res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush, ctx=a.ctx)
     res["device_error"] = L.device_error()
     print(json.dumps(res))
 
