@@ -51,10 +51,10 @@ def test_attention_matches_fp32(cuda, B, T, H):
 
 
 @pytest.mark.parametrize("B,T,H", [(64, 512, 20), (40, 300, 1), (149, 200, 1), (300, 150, 1),
-                                   (4, 1152, 20), (4, 1153, 20)])
+                                   (4, 1280, 20), (4, 1344, 20), (4, 1345, 20)])
 def test_attention_persistent_many_items(cuda, B, T, H):
-    """Items of at most 12 key blocks (T <= 1152) run on the persistent kernel,
-    one CTA per SM walking several (tile pair, head, clip) items; 1153 is the
+    """Items of at most 14 key blocks (T <= 1344) run on the persistent kernel,
+    one CTA per SM walking several (tile pair, head, clip) items; 1345 is the
     first length on the per-item kernel. Checked per clip against fp32, and
     equal bit for bit to the same clips run one at a time (one clip has fewer
     items than SMs, so there every CTA takes a single item): carrying the

@@ -19,7 +19,8 @@
 // loop (at the 96-register cap of 19 warps some spill), which costs a little
 // per key block, so it runs only short items, where the fixed cost dominates
 // (kAttPersistMaxBlocks; measured at 64 clips x 20 heads: T 512 +15%, 768
-// +10%, 1024 +3.5%, 1152 +2%; at 1280 and 1500 the per-item kernel is faster).
+// +10%, 1024 +3.5%, 1152 +2%, 1280 +1.5%, 1344 even; at 1500 the per-item
+// kernel is 1% faster).
 // Both compute the same arithmetic in the same order: outputs are identical.
 // 19 warps in both:
 //   warp 0     TMA: the two Q tiles of an item, then K and V tiles (96 keys
@@ -108,8 +109,8 @@ constexpr int kAttSmem = 1024 + 2 * kQBytes + 2 * kAttStages * kKVBytes + kAttBa
                          2 * 2 * 2 * 128 * 4;
 // the persistent kernel: a second Q buffer
 constexpr int kAttSmemPersist = kAttSmem + 2 * kQBytes;
-// the persistent kernel for items of at most this many key blocks (T <= 1152)
-constexpr int kAttPersistMaxBlocks = 12;
+// the persistent kernel for items of at most this many key blocks (T <= 1344)
+constexpr int kAttPersistMaxBlocks = 14;
 constexpr int kAttTmemCols = 512;
 constexpr int kSBufCols = kAttBK;                 // one S buffer: 96 fp32 columns
 constexpr int kOCol = 4 * kSBufCols;              // O_A at 384, O_B at 448

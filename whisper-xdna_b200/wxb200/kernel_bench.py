@@ -172,7 +172,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--flush", action="store_true")
     ap.add_argument("--ctx", type=int, default=T,
-                    help="attention only: frames per clip (T <= 1152 runs the persistent kernel)")
+                    help="attention only: frames per clip (T <= 1344 runs the persistent kernel)")
     a = ap.parse_args()
     res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush, ctx=a.ctx)
     res["device_error"] = L.device_error()
