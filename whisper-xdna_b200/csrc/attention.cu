@@ -22,7 +22,11 @@
 // +10%, 1024 +3.5%, 1152 +2%, 1280 +1.5%, 1344 even; at 1500 the per-item
 // kernel is 1% faster).
 // Both compute the same arithmetic in the same order: outputs are identical.
-// 19 warps in both:
+// They are two functions rather than one template on purpose: a template whose
+// per-item instance folds the item loops away compiled spill-free but ran 5-6%
+// slower than this per-item source at T >= 1280 (the kernel sits at the
+// register cap, where small code changes move its schedule), so the per-item
+// kernel keeps its own code. 19 warps in both:
 //   warp 0     TMA: the two Q tiles of an item, then K and V tiles (96 keys
 //              x 64) into three-slot rings with separate K and V barriers
 //   warps 1-2  MMA issuers, one per query tile (warp 1 also allocates tensor
