@@ -46,3 +46,14 @@ def test_synthetic_weights_have_the_reference_layout():
     w = W["w.blocks.0.mlp.0.weight"]
     assert abs(float(w.std()) - 0.02) < 1e-3                          # N(0, 0.02)
     assert np.array_equal(w, w.astype(np.float32).view(np.uint32).__and__(0xFFFF0000).view(np.float32))
+
+
+def test_kernel_bench_attention_work_follows_ctx():
+    """kernel_bench's attention FLOP and byte counts at any frame count (its
+    --ctx option; the persistent kernel runs T <= 1344): 4 B T^2 d FLOP, and
+    Q, K, V read and O written once, 2 bytes each."""
+    from wxb200 import kernel_bench as KB
+    for ctx in (1500, 512):
+        _, flop, byt = KB.setup("attention", 2, dev="cpu", ctx=ctx)
+        assert flop == 4.0 * 2 * ctx * ctx * 1280
+        assert byt == 4.0 * 2 * ctx * 1280 * 2
