@@ -14,8 +14,12 @@ checkpoint or audio can be fetched here).
 --impl reference times the reference's own CPU implementation of the path --
 its numpy encoder (src/npu_whisper_encoder.py:encoder with np_matmul),
 restated in oracle/encoder_ref.py because the reference's Python cannot travel
-to the GPU box -- on the host cores, one clip per step over a bounded number
-of layers, extrapolated to the 32-layer clip.
+to the GPU box -- on all the host cores, one whole 32-layer clip per step.
+
+Beside the weak-scaling value the line carries `fixed_global_batch`: the same
+loop with one global batch (--global-batch, default 64) split into contiguous
+per-GPU slices (strong scaling), and `per_rank`: every rank's own step time,
+SM clock and power, so the rank that limits the max-over-ranks time is named.
 """
 import argparse
 import json
@@ -49,6 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=64, help="clips per GPU per step")
+    ap.add_argument("--global-batch", type=int, default=64,
+                    help="fixed-batch leg: this many clips per step split across the GPUs")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quant", choices=["none", "int8-perchan", "int8-pertensor"],
@@ -112,8 +118,15 @@ def cpu_cores():
 def run_reference(args, rank):
     if rank != 0:
         return
-    # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    # All host threads. torchrun gives each worker OMP_NUM_THREADS=1, and the
+    # BLAS libraries read their thread count when they load, so the variables
+    # are set before numpy or torch is first imported (nothing above imports
+    # either); the limits are applied again once they are loaded.
     n = os.cpu_count() or 1
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = str(n)
+    import torch
+    torch.set_num_threads(n)
     try:
         from threadpoolctl import threadpool_limits
         threadpool_limits(limits=n)
@@ -174,7 +187,7 @@ class Clocks:
         except Exception:
             self.proc.kill()
             out = ""
-        sm, mx, reasons = [], None, set()
+        sm, mx, pw, reasons = [], None, [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
             f = [x.strip() for x in line.split(",")]
@@ -185,11 +198,16 @@ class Clocks:
                 mx = float(f[2])
             except ValueError:
                 continue
+            try:
+                pw.append(float(f[3]))
+            except ValueError:
+                pass
             for name, val in zip(names, f[5:9]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(pw) if pw else None}
 
 
 def make_weights_fast(seed):
@@ -301,8 +319,39 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
-    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    t_rank = e0.elapsed_time(e1) / 1e3
+    t_dev = max_over_ranks(t_rank)
     finite = bool(torch.isfinite(out).all().item())
+    # which rank limits the job: each rank's own step time, clock and power
+    per_rank = wdist.gather_to_all({
+        "rank": rank, "ms_per_step": t_rank / args.steps * 1e3, "sm_mhz": clk.get("sm_mhz"),
+        "power_w_max": clk.get("power_w_max"), "reasons": clk.get("reasons")})
+
+    # ---- fixed global batch (BASELINE batch-64 config with the clips sharded
+    # across the GPUs): each rank encodes its contiguous slice of the same
+    # global batch (wxb200.dist.shard), so per-GPU work shrinks as N grows
+    gb = args.global_batch
+    lo, hi = wdist.shard(gb, world, rank)
+    nloc = hi - lo
+    t_fixed_rank = 0.0
+    if nloc > 0:
+        mel_s, out_s = mel[:nloc], out[:nloc]
+        for _ in range(args.warmup):
+            enc.forward(mel_s, out=out_s)
+        torch.cuda.synchronize()
+    barrier()
+    if nloc > 0:
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(st)
+        for _ in range(args.steps):
+            enc.forward(mel_s, out=out_s)
+        f1.record(st)
+        torch.cuda.synchronize()
+        t_fixed_rank = f0.elapsed_time(f1) / 1e3
+    barrier()
+    t_fixed = max_over_ranks(t_fixed_rank)
+    fixed_per_rank = wdist.gather_to_all({"rank": rank, "clips": nloc,
+                                          "ms_per_step": t_fixed_rank / args.steps * 1e3})
 
     # the ctx-512 variant of the same configuration: each clip's mel cut to its
     # first 1024 frames (bench/run_raw_encoder.py:63-65), the same clips
@@ -429,6 +478,13 @@ def run_b200(args, rank, world, local_rank):
                              else (3 + 3 + 9 * N_LAYER + 1 + 1)) * args.steps,
             "roofline": roof, "kernels": kernels, "row_ops": row_ops, "clocks": clk,
             "batch1_latency": lat,
+            "per_rank": per_rank,
+            "fixed_global_batch": {
+                "value": gb * args.steps / t_fixed, "unit": UNIT, "global_batch": gb,
+                "ms_per_step": t_fixed / args.steps * 1e3, "scaling": "strong",
+                "per_rank": fixed_per_rank,
+                "note": "the same timed loop with one global batch split into contiguous "
+                        "per-GPU slices (wxb200.dist.shard); max over ranks"},
             "ctx512": {"value": B * world * args.steps / t_512, "unit": UNIT,
                        "ms_per_clip_per_gpu": t_512 / args.steps * 1e3 / B,
                        "flop_per_clip": FLOP_PER_CLIP_512,

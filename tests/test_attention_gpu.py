@@ -1,9 +1,14 @@
 """Fused tcgen05 attention against a plain torch fp32 reference of the same
 op (bf16 Q, K, V; fp32 math), through the C ABI.
 
-Bar: max |O - O_ref| <= 2e-2 * max|V| and relative L2 <= 1e-2 (P is rounded to
-bf16 before the PV product, and O is stored in bf16; the reference's own
-chain measured rel L2 0.0068, README.md:223). Known answers from the
+Bars sit near the errors measured on a B200, with about a 2x margin (every
+check prints its MEASURED values): relative L2 < 5e-3 (measured 2.2e-3 to
+2.35e-3 on every shape; P is rounded to bf16 before the PV product, and O is
+stored in bf16) and max |O - O_ref| <= 1.5e-3 * max|V| (measured at most
+6.5e-4). The reference's own chain measured rel L2 0.0068 and its fused
+kernel 0.0088 (README.md:223). Logits six times larger (the large-logits
+case) measured rel L2 1.3e-3 and max error 5.0e-3 * max|V|; its bars are
+3e-3 and 1e-2. Known answers from the
 reference's history: K = 0 makes attention uniform, so every output row is the
 column mean of V (HISTORY.md:220-223); V = ones gives ones.
 """
@@ -34,10 +39,13 @@ def ref_attention(qkv, B, T, H, scale, hd=64):
     return (p @ v).transpose(1, 2).reshape(B * T, d)
 
 
-def check(got, ref, v):
+def check(got, ref, v, tag="", l2_bar=5e-3, max_bar=1.5e-3):
     diff = (got.float() - ref).abs()
-    assert diff.max().item() <= 2e-2 * v.float().abs().max().item()
-    assert (torch.linalg.norm(got.float() - ref) / torch.linalg.norm(ref)).item() < 1e-2
+    rel_max = diff.max().item() / v.float().abs().max().item()
+    rel_l2 = (torch.linalg.norm(got.float() - ref) / torch.linalg.norm(ref)).item()
+    print(f"MEASURED attention {tag}: rel L2 {rel_l2:.3e}, max err / max|V| {rel_max:.3e}")
+    assert rel_max <= max_bar, (tag, rel_max)
+    assert rel_l2 < l2_bar, (tag, rel_l2)
 
 
 @pytest.mark.parametrize("B,T,H", [(1, 1500, 6), (1, 1500, 20), (2, 1500, 6), (16, 1500, 6),
@@ -47,7 +55,7 @@ def test_attention_matches_fp32(cuda, B, T, H):
     qkv = qkv_rand(B, T, H, B * 1000 + T + H)
     d = H * 64
     got = A.attn_heads(qkv, H, scale=1 / 8, n_batch=B)
-    check(got, ref_attention(qkv, B, T, H, 1 / 8), qkv[:, 2 * d:])
+    check(got, ref_attention(qkv, B, T, H, 1 / 8), qkv[:, 2 * d:], f"B{B} T{T} H{H}")
 
 
 @pytest.mark.parametrize("B,T,H", [(64, 512, 20), (40, 300, 1), (149, 200, 1), (300, 150, 1),
@@ -64,7 +72,8 @@ def test_attention_persistent_many_items(cuda, B, T, H):
     got = A.attn_heads(qkv, H, scale=1 / 8, n_batch=B)
     for b in range(0, B, max(1, B // 4)):
         rows = slice(b * T, (b + 1) * T)
-        check(got[rows], ref_attention(qkv[rows], 1, T, H, 1 / 8), qkv[rows, 2 * d:])
+        check(got[rows], ref_attention(qkv[rows], 1, T, H, 1 / 8), qkv[rows, 2 * d:],
+              f"persistent B{B} T{T} H{H} clip {b}")
     per_clip = torch.cat([A.attn_heads(qkv[b * T:(b + 1) * T], H, scale=1 / 8) for b in range(B)])
     assert torch.equal(got, per_clip)
 
@@ -88,7 +97,7 @@ def test_attention_batch16_large(cuda):
     d = H * 64
     got = A.attn_heads(qkv, H, n_batch=B)
     ref = torch.cat([ref_attention(qkv[b * T:(b + 1) * T], 1, T, H, 1 / 8) for b in range(B)])
-    check(got, ref, qkv[:, 2 * d:])
+    check(got, ref, qkv[:, 2 * d:], "B16 T1500 H20")
 
 
 def test_attention_large_logits(cuda):
@@ -96,7 +105,8 @@ def test_attention_large_logits(cuda):
     B, T, H = 1, 700, 2
     qkv = (qkv_rand(B, T, H, 5).float() * 6).to(torch.bfloat16)
     d = H * 64
-    check(A.attn_heads(qkv, H, scale=1 / 8), ref_attention(qkv, B, T, H, 1 / 8), qkv[:, 2 * d:])
+    check(A.attn_heads(qkv, H, scale=1 / 8), ref_attention(qkv, B, T, H, 1 / 8), qkv[:, 2 * d:],
+          "large logits", l2_bar=3e-3, max_bar=1e-2)
 
 
 def test_attention_zero_keys_gives_column_mean(cuda):

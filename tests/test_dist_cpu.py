@@ -39,7 +39,8 @@ def _worker(rank, world, port, q):
         w, r = D.world()
         t = D.max_over_ranks(1.0 + rank)          # rank 1 is the slow one
         clips = D.sum_over_ranks(D.shard(64, w, r)[1] - D.shard(64, w, r)[0])
-        q.put((rank, w, r, t, clips))
+        per_rank = D.gather_to_all({"rank": rank, "ms": 10.0 * (rank + 1)})
+        q.put((rank, w, r, t, clips, per_rank))
     finally:
         dist.destroy_process_group()
 
@@ -55,7 +56,8 @@ def test_two_gloo_ranks_barrier_max_and_shards():
         p.join(timeout=120)
         assert p.exitcode == 0
     out = sorted(q.get(timeout=10) for _ in range(2))
-    for rank, w, r, t, clips in out:
+    for rank, w, r, t, clips, per_rank in out:
         assert (w, r) == (2, rank)
         assert t == 2.0          # max over ranks
         assert clips == 64       # the shards add up to the batch
+        assert per_rank == [{"rank": 0, "ms": 10.0}, {"rank": 1, "ms": 20.0}]

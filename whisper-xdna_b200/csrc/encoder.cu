@@ -565,6 +565,7 @@ int wx_encoder_create(wx_encoder** out, int n_mels, int d_model, int n_head, int
 
 int wx_encoder_destroy(wx_encoder* e) {
   if (!e) return WX_OK;
+  DeviceGuard dg(e->device);
   // submitted batches finish writing their host buffers first
   for (int k = 0; k < 2; k++)
     if (e->q_busy[k]) cudaEventSynchronize(e->ev_q_out[k]);
@@ -592,6 +593,7 @@ int wx_encoder_destroy(wx_encoder* e) {
 int wx_encoder_set_frontend(wx_encoder* e, const float* conv1_w, const float* conv1_b,
                             const float* conv2_w, const float* conv2_b, const float* pos) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  DeviceGuard dg(e->device);
   const int64_t d = e->d;
   if (e->quant) {
     const int64_t k1 = 3 * (int64_t)e->n_mels;
@@ -614,6 +616,7 @@ int wx_encoder_set_layer(wx_encoder* e, int layer, const float* attn_ln_w, const
                          const float* mlp_ln_b, const float* w1, const float* b1, const float* w2,
                          const float* b2) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  DeviceGuard dg(e->device);
   if (layer < 0 || layer >= e->nl) return fail(WX_ERR_INVALID, "encoder: layer %d", layer);
   const int64_t d = e->d, ffn = e->ffn;
   LayerW& w = e->L[layer];
@@ -648,6 +651,7 @@ int wx_encoder_set_layer(wx_encoder* e, int layer, const float* attn_ln_w, const
 
 int wx_encoder_set_quant(wx_encoder* e, int mode) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  DeviceGuard dg(e->device);
   if (mode != WX_QUANT_NONE && mode != WX_QUANT_INT8_PERCHAN && mode != WX_QUANT_INT8_PERTENSOR)
     return fail(WX_ERR_INVALID, "encoder_set_quant: mode %d", mode);
   if (e->set_front || e->set_post || std::find(e->set_layer.begin(), e->set_layer.end(), true) !=
@@ -698,6 +702,7 @@ int wx_encoder_set_quant(wx_encoder* e, int mode) {
 
 int wx_encoder_set_ln_post(wx_encoder* e, const float* w, const float* b) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  DeviceGuard dg(e->device);
   WX_TRY(upload_f32(e, e->lnp_g, w, e->d));
   WX_TRY(upload_f32(e, e->lnp_b, b, e->d));
   e->set_post = true;
@@ -709,6 +714,7 @@ int64_t wx_encoder_device_bytes(const wx_encoder* e) { return e ? e->bytes : 0; 
 int wx_encoder_forward(wx_encoder* e, const float* mel, float* out, int64_t batch,
                        int64_t n_frames, int use_graph, void* stream) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  DeviceGuard dg(e->device);
   if (!mel || !out) return fail(WX_ERR_INVALID, "encoder_forward: NULL buffer");
   if (batch <= 0 || batch > e->max_batch)
     return fail(WX_ERR_INVALID, "encoder_forward: batch %lld not in [1, %d]", (long long)batch, e->max_batch);
@@ -772,6 +778,7 @@ int wx_encoder_forward(wx_encoder* e, const float* mel, float* out, int64_t batc
 int wx_encoder_forward_host(wx_encoder* e, const float* mel_host, float* out_host, int64_t batch,
                             int64_t n_frames, int use_graph, void* stream) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  DeviceGuard dg(e->device);
   if (!mel_host || !out_host) return fail(WX_ERR_INVALID, "encoder_forward_host: NULL buffer");
   if (batch <= 0 || batch > e->max_batch || n_frames <= 0 || n_frames % 2 ||
       n_frames / 2 > e->n_ctx)
@@ -815,6 +822,7 @@ int wx_encoder_forward_host(wx_encoder* e, const float* mel_host, float* out_hos
 int wx_encoder_submit_host(wx_encoder* e, const float* mel_host, float* out_host, int64_t batch,
                            int64_t n_frames, int use_graph) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  DeviceGuard dg(e->device);
   if (!mel_host || !out_host) return fail(WX_ERR_INVALID, "encoder_submit_host: NULL buffer");
   if (batch <= 0 || batch > e->max_batch || n_frames <= 0 || n_frames % 2 ||
       n_frames / 2 > e->n_ctx)
@@ -855,6 +863,7 @@ int wx_encoder_submit_host(wx_encoder* e, const float* mel_host, float* out_host
 
 int wx_encoder_wait_host(wx_encoder* e) {
   if (!e) return fail(WX_ERR_INVALID, "encoder: NULL handle");
+  DeviceGuard dg(e->device);
   for (int k = 0; k < 2; k++) {
     if (!e->q_busy[k]) continue;
     e->q_busy[k] = false;

@@ -49,4 +49,20 @@ int sm_count();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Makes `dev` the calling thread's current device for a scope and restores
+// the caller's device after: an engine's entry points run on the device the
+// engine was created on, whichever device the calling thread has current.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess || prev == dev || cudaSetDevice(dev) != cudaSuccess)
+      prev = -1;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+
 }  // namespace wx

@@ -51,3 +51,14 @@ def sum_over_ranks(value, device=None):
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
+
+
+def gather_to_all(obj):
+    """Every rank's `obj` (picklable), in rank order, on every rank; [obj] when
+    not distributed. Used for the per-rank timing and clock records the
+    benchmark prints beside the max-over-ranks time."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [obj]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, obj)
+    return out

@@ -115,20 +115,23 @@ class Encoder:
         return int(L.lib().wx_encoder_device_bytes(self._h))
 
     def forward(self, mel, out=None, use_graph=True):
-        """mel: CUDA fp32 (batch, n_mels, n_frames) (or (n_mels, n_frames)) ->
-        (batch, n_frames // 2, d) fp32 CUDA tensor, on torch's current stream."""
+        """mel: CUDA fp32 (batch, n_mels, n_frames) (or (n_mels, n_frames)) on this
+        encoder's device -> (batch, n_frames // 2, d) fp32 CUDA tensor, on torch's
+        current stream of that device."""
         squeeze = mel.dim() == 2
         if squeeze:
             mel = mel.unsqueeze(0)
         if not mel.is_cuda or mel.dtype != torch.float32:
             raise ValueError("mel must be a float32 CUDA tensor")
+        if mel.device != self.device:
+            raise ValueError(f"mel is on {mel.device}, the encoder on {self.device}")
         mel = mel.contiguous()
         B, C, F = mel.shape
         if C != self.n_mels:
             raise ValueError(f"mel has {C} bins, the weights expect {self.n_mels}")
         if out is None:
             out = torch.empty(B, F // 2, self.d, dtype=torch.float32, device=mel.device)
-        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        st = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         L.check(L.lib().wx_encoder_forward(self._h, ctypes.c_void_p(mel.data_ptr()),
                                            ctypes.c_void_p(out.data_ptr()), B, F,
                                            1 if use_graph else 0, st))
@@ -148,7 +151,13 @@ class Encoder:
             raise ValueError(f"mel has {C} bins, the weights expect {self.n_mels}")
         if out is None:
             out = np.empty((B, F // 2, self.d), dtype=np.float32)
-        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        elif squeeze and out.shape == (F // 2, self.d):
+            out = out[None]
+        if (not isinstance(out, np.ndarray) or out.dtype != np.float32
+                or out.shape != (B, F // 2, self.d) or not out.flags.c_contiguous):
+            raise ValueError(f"out must be a C-contiguous float32 array of shape "
+                             f"{(B, F // 2, self.d)}")
+        st = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
         L.check(L.lib().wx_encoder_forward_host(self._h, mel.ctypes.data_as(ctypes.c_void_p),
                                                 out.ctypes.data_as(ctypes.c_void_p), B, F,
                                                 1 if use_graph else 0, st))
