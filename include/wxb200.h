@@ -190,9 +190,10 @@ int wx_attention(const void* q, const void* k, const void* v, void* o, int64_t B
 /* ------------------------------------------------------------ no allocation */
 
 /* The MLP block out = GELU(h @ w1^T + b1) @ w2^T + b2 for callers that cannot
- * allocate device memory -- code running under CUDA graph capture, processes
- * whose device memory belongs to another allocator, callers that must not
- * allocate after start-up. It has no counterpart in the reference.
+ * allocate device memory -- processes whose device memory belongs to another
+ * allocator (a framework's caching allocator, a fixed memory plan), and
+ * callers that must not allocate after start-up. It has no counterpart in the
+ * reference.
  * h (M x d, bf16, row stride ldh), w1 (ffn x d) and w2 (d x ffn) bf16 in the
  * torch Linear layout, b1 (ffn) and b2 (d) fp32 or NULL, out (M x d) fp32 with
  * row stride ldo; gelu_mode WX_GELU_POLY4 or WX_GELU_ERF. The fc1 activation
@@ -202,8 +203,9 @@ int wx_attention(const void* q, const void* k, const void* v, void* o, int64_t B
  * library routine here. The array's device address is looked up on the first
  * call on each device (cudaGetSymbolAddress), so make that first call before
  * any stream capture. Every call shares the array: calls that overlap on the
- * GPU race on it. Device-side waits that give up are not recorded in the
- * wx_device_error word on this path. */
+ * GPU race on it. A device-side wait that gives up records WX_DEVERR_TIMEOUT
+ * in an error word of this path (a file-scope device variable, not an
+ * allocation), which wx_device_error reports and clears with the library's. */
 int wx_mlp_bf16_noalloc(const void* h, const void* w1, const float* b1, const void* w2,
                         const float* b2, float* out, int64_t M, int64_t d, int64_t ffn,
                         int64_t ldh, int64_t ldo, int gelu_mode, void* stream);

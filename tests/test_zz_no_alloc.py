@@ -1,14 +1,16 @@
 """The allocation-free MLP entry point, wx_mlp_bf16_noalloc, through the C ABI.
 
-It exists for callers that cannot call cudaMalloc -- code running while a CUDA
-graph is being captured, processes whose device memory belongs to another
-allocator, callers that must not allocate after start-up -- and keeps the fc1
-activation in the library's fixed device array instead of memory the caller
-provides. Its result must equal the same computation through the existing
-entry point (wx_gemm_bf16 for fc1 + GELU into a caller buffer, then for fc2)
-on two calls in a row with different inputs, so the shared array cannot hand
-one call's activation to the next. This file is named to be collected last
-and passes alone in a fresh process as well as after the other tests.
+It exists for callers that cannot call cudaMalloc -- processes whose device
+memory belongs to another allocator, callers that must not allocate after
+start-up -- and keeps the fc1 activation in the library's fixed device array
+instead of memory the caller provides. Its result must equal the same
+computation through the existing entry point (wx_gemm_bf16 for fc1 + GELU
+into a caller buffer, then for fc2) on two calls in a row with different
+inputs, so the shared array cannot hand one call's activation to the next.
+A call after the first one leaves the device's free memory unchanged, and no
+bounded wait of its kernels reports a timeout (wx_device_error covers this
+path's own error word). This file is named to be collected last and passes
+alone in a fresh process as well as after the other tests.
 """
 import ctypes
 
@@ -67,6 +69,26 @@ def test_noalloc_matches_existing_entry_point_twice(M, d, ffn, gelu_mode, gelu_e
         err = (got - ref).abs().max().item() / ref.abs().max().item()
         assert err < 1e-5, (call, err)           # the GEMM tests' fp32 bar
         assert torch.equal(got, ref), call       # same kernels: identical in practice
+    assert L.device_error() == 0
+
+
+def test_noalloc_warm_call_leaves_free_memory_unchanged():
+    M, d, ffn = 1500, 1280, 5120
+    h, w1, b1, w2, b2 = inputs(M, d, ffn, 7)
+    out = torch.empty(M, d, device="cuda")
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def call():
+        L.check(L.lib().wx_mlp_bf16_noalloc(p(h), p(w1), p(b1), p(w2), p(b2), p(out), M, d,
+                                            ffn, d, d, L.WX_GELU_POLY4, st))
+        torch.cuda.synchronize()
+
+    call()                                        # first call on the device: set-up
+    free0, _ = torch.cuda.mem_get_info()
+    call()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert L.device_error() == 0
 
 
 def test_noalloc_rejects_sizes_beyond_the_scratch():

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "plans.cuh"
 #include "wxb200_internal.h"
 
 namespace wx {
@@ -114,7 +115,8 @@ int wx_device_error(int* flags, int clear) {
   WX_CUDA_TRY(cudaDeviceSynchronize());
   WX_CUDA_TRY(cudaMemcpy(flags, w, sizeof(int), cudaMemcpyDeviceToHost));
   if (clear) WX_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
-  return WX_OK;
+  // the allocation-free entry point records into a word of its own
+  return wx::noalloc_take_error(flags, clear != 0);
 }
 
 }  // extern "C"

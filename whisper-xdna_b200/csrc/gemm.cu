@@ -906,10 +906,12 @@ static int encode_epilogue_maps(GemmPlan* p, void* C, const float* R, int64_t M,
   return WX_OK;
 }
 
+// err: the error word the kernels' bounded waits record into; NULL takes the
+// library's per-device word (device_error_word(), allocated on first use).
 static int gemm_plan_impl(GemmPlan* p, const void* A, const void* B, const float* bias,
                           const float* R, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                           int64_t ldb, int64_t ldc, int64_t ldr, int epi, int force_bn, bool i8,
-                          const float* sa, const float* sw, float* rowmax) {
+                          const float* sa, const float* sw, float* rowmax, int* err) {
   if (M <= 0 || N <= 0 || K <= 0) return fail(WX_ERR_INVALID, "gemm: M, N, K must be > 0");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
     return fail(WX_ERR_UNSUPPORTED, "gemm: dimension exceeds 2^31");
@@ -938,7 +940,7 @@ static int gemm_plan_impl(GemmPlan* p, const void* A, const void* B, const float
   if (bn == 0) bn = (mb * ((N + 255) / 256) >= nsm && N > 128) ? 256 : 128;
   if (bn != 128 && bn != 256) return fail(WX_ERR_INVALID, "gemm: BN %d", bn);
   const bool pair = force_bn == 0 && use_pair(M, N, nsm);
-  int* err = device_error_word();
+  if (!err) err = device_error_word();
   if (!err) return fail(WX_ERR_CUDA, "gemm: device error word unavailable");
   // one K step is 128 bytes of every row: 64 bf16 or 128 int8 elements
   const CUtensorMapDataType dt = i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -985,72 +987,25 @@ int gemm_plan(GemmPlan* p, const void* A, const void* B, const float* bias, cons
               void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
               int64_t ldr, int epi, int force_bn) {
   return gemm_plan_impl(p, A, B, bias, R, C, M, N, K, lda, ldb, ldc, ldr, epi, force_bn, false,
-                        nullptr, nullptr, nullptr);
+                        nullptr, nullptr, nullptr, nullptr);
 }
 
 int gemm_plan_i8(GemmPlan* p, const void* A, const void* B, const float* sa, const float* sw,
                  const float* bias, const float* R, void* C, int64_t M, int64_t N, int64_t K,
                  int64_t lda, int64_t ldb, int64_t ldc, int64_t ldr, int epi, float* rowmax) {
   return gemm_plan_impl(p, A, B, bias, R, C, M, N, K, lda, ldb, ldc, ldr, epi, 0, true, sa, sw,
-                        rowmax);
+                        rowmax, nullptr);
 }
 
-// The same plan without the library's device error word, whose first use on
-// a device allocates it: the kernels' bounded waits then record nothing. Used
-// only by the allocation-free entry point (noalloc.cu).
-int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, const float* bias,
-                                 void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                                 int64_t ldb, int64_t ldc, int epi) {
-  if (M <= 0 || N <= 0 || K <= 0) return fail(WX_ERR_INVALID, "gemm: M, N, K must be > 0");
-  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
-    return fail(WX_ERR_UNSUPPORTED, "gemm: dimension exceeds 2^31");
-  if (!A || !B || !C) return fail(WX_ERR_INVALID, "gemm: NULL operand");
-  if (epi != WX_EPI_F32 && epi != WX_EPI_BF16 && epi != WX_EPI_BF16_GELU &&
-      epi != WX_EPI_BF16_GELU_ERF)
-    return fail(WX_ERR_INVALID, "gemm: epilogue %d", epi);
-  if (lda < K || ldb < K || ldc < N) return fail(WX_ERR_INVALID, "gemm: leading dimension too small");
-  if (lda % 8 || ldb % 8) return fail(WX_ERR_INVALID, "gemm: lda and ldb must be multiples of 8");
-  if (ldc % (epi == WX_EPI_F32 ? 4 : 8))
-    return fail(WX_ERR_INVALID, "gemm: ldc must keep rows 16-byte aligned");
-  if ((reinterpret_cast<uintptr_t>(C) & 15) || (bias && (reinterpret_cast<uintptr_t>(bias) & 15)))
-    return fail(WX_ERR_INVALID, "gemm: C and bias must be 16-byte aligned");
-  const int nsm = sm_count();
-  const int64_t mb = (M + kGemmBM - 1) / kGemmBM;
-  const int bn = (mb * ((N + 255) / 256) >= nsm && N > 128) ? 256 : 128;  // as gemm_plan
-  const bool pair = use_pair(M, N, nsm);
-  WX_TRY(encode_tensor_map_2d(&p->tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
-                              (uint64_t)M, (uint64_t)lda * 2, kGemmBK, kGemmBM,
-                              CU_TENSOR_MAP_SWIZZLE_128B));
-  WX_TRY(encode_tensor_map_2d(&p->tmB, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
-                              (uint64_t)N, (uint64_t)ldb * 2, kGemmBK, pair ? 128u : (uint32_t)bn,
-                              CU_TENSOR_MAP_SWIZZLE_128B));
-  GemmArgs& g = p->args;
-  g.M = (int)M;
-  g.N = (int)N;
-  g.K = (int)K;
-  g.num_n_blocks = (int)((N + bn - 1) / bn);
-  g.num_tiles = (int)((pair ? (M + 255) / 256 : mb) * g.num_n_blocks);
-  g.num_k_blocks = (int)((K + kGemmBK - 1) / kGemmBK);
-  g.C = C;
-  g.ldc = ldc;
-  g.bias = bias;
-  g.R = nullptr;
-  g.ldr = 0;
-  g.err = nullptr;
-  g.pos = nullptr;
-  g.ldp = 0;
-  g.pos_T = 1;
-  g.sa = nullptr;
-  g.sw = nullptr;
-  g.rowmax = nullptr;
-  g.resid_inplace = 0;
-  p->bn = bn;
-  p->epi = epi;
-  p->pair = pair;
-  p->i8 = false;
-  p->grid = pair ? 2 * std::min(g.num_tiles, nsm / 2) : std::min(g.num_tiles, nsm);
-  WX_TRY(encode_epilogue_maps(p, C, nullptr, M, N, ldc, 0, epi));
-  return gemm_prepare(bn, epi, pair, false);
+// The same bf16 plan recording its kernels' wait timeouts into `err`, a word
+// the caller owns (the allocation-free entry point's, in noalloc.cu), instead
+// of the library's per-device word, whose first use on a device allocates it.
+int gemm_plan_err(GemmPlan* p, const void* A, const void* B, const float* bias, void* C,
+                  int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int epi,
+                  int* err) {
+  if (!err) return fail(WX_ERR_INVALID, "gemm: NULL error word");
+  return gemm_plan_impl(p, A, B, bias, nullptr, C, M, N, K, lda, ldb, ldc, 0, epi, 0, false,
+                        nullptr, nullptr, nullptr, err);
 }
 
 template <int BN, int EPI, bool I8>

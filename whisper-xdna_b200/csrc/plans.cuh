@@ -51,9 +51,14 @@ int gemm_plan_i8(GemmPlan* p, const void* A, const void* B, const float* sa, con
                  const float* bias, const float* R, void* C, int64_t M, int64_t N, int64_t K,
                  int64_t lda, int64_t ldb, int64_t ldc, int64_t ldr, int epi, float* rowmax);
 int gemm_run(const GemmPlan& p, cudaStream_t st);
-int gemm_plan_without_error_word(GemmPlan* p, const void* A, const void* B, const float* bias,
-                                 void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                                 int64_t ldb, int64_t ldc, int epi);
+// A bf16 plan whose kernels record wait timeouts into `err` (a word the
+// caller owns) instead of the library's per-device error word.
+int gemm_plan_err(GemmPlan* p, const void* A, const void* B, const float* bias, void* C,
+                  int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int epi,
+                  int* err);
+// The allocation-free entry point's error word on the current device (if it
+// has been set up there): OR it into *flags, and clear it when asked.
+int noalloc_take_error(int* flags, bool clear);
 // attach the positional embedding to a plan built with kEpiF32Gelu*Pos
 void gemm_set_pos(GemmPlan* p, const float* pos, int64_t ldp, int pos_T);
 
