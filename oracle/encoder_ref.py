@@ -210,12 +210,6 @@ def encoder_np(W, mel, n_layer=None, n_head=None):
     return layer_norm_np(x, W["w.ln_post.weight"], W["w.ln_post.bias"])
 
 
-def encoder_np_partial(W, mel, n_layer, n_head):
-    """Frontend + the first n_layer blocks + ln_post: the bounded CPU sample the
-    benchmark times (one clip, a few layers)."""
-    return encoder_np(W, mel, n_layer=n_layer, n_head=n_head)
-
-
 # ------------------------------------------------------------------ torch path
 
 def encoder_torch(W, mel, n_layer=None, n_head=None, threads=None):

@@ -20,6 +20,7 @@ KERNELS = {
     "g4r": ("gelu_row4_rne.so", "gelu_row4_bf16", "bf16"),
     "g4f": ("gelu_row4f.so", "gelu_row4f_bf16", "f32"),
     "s1": ("softmax_row.so", "softmax_row_bf16", "bf16"),
+    "s2": ("softmax_row2.so", "softmax_row2_bf16", "bf16"),
     "s3": ("softmax_row3.so", "softmax_row3_bf16", "bf16"),
     "s4": ("softmax_row4.so", "softmax_row4_bf16", "bf16"),
     "s4r": ("softmax_row4_rne.so", "softmax_row4r_bf16", "bf16"),

@@ -13,6 +13,7 @@ synthetic weights and mel from oracle/encoder_ref.py. Only the inputs' seeds and
 the reference's outputs are stored: the tests regenerate the inputs from the
 seeds, so the fixtures stay small.
 """
+import os
 import sys
 from pathlib import Path
 
@@ -52,4 +53,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference checkout: first argument, else $WX_REFERENCE_DIR, else a
+    # checkout named "reference" beside this repository
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get(
+        "WX_REFERENCE_DIR", str(REPO.parent / "reference")))

@@ -19,6 +19,7 @@ Stored: the seeds of the inputs and the reference's outputs.
   quant_enc_*.npz    the encoder's output with q_matmul_factory(mode) as mm
 """
 import ast
+import os
 import sys
 from pathlib import Path
 
@@ -88,4 +89,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference checkout: first argument, else $WX_REFERENCE_DIR, else a
+    # checkout named "reference" beside this repository
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get(
+        "WX_REFERENCE_DIR", str(REPO.parent / "reference")))

@@ -118,10 +118,14 @@ def test_gelu_f32_oracle_bit_exact_to_reference_source():
 
 
 @needs_ref
-@pytest.mark.parametrize("op,variant,mode", [("s1", 1, O.TRUNC), ("s3", 3, O.TRUNC),
-                                             ("s4", 4, O.TRUNC), ("s4r", 4, O.RNE)])
+@pytest.mark.parametrize("op,variant,mode", [("s1", 1, O.TRUNC), ("s2", 4, O.TRUNC),
+                                             ("s3", 3, O.TRUNC), ("s4", 4, O.TRUNC),
+                                             ("s4r", 4, O.RNE)])
 @pytest.mark.parametrize("valid", [0, 1504])
 def test_softmax_oracle_bit_exact_to_reference_source(op, variant, mode, valid):
+    """softmax_row2.cc (s2) is checked against the v4 restatement: the two
+    kernels compute the same arithmetic, which is why rowops.softmax_row2
+    runs the v4 device kernel."""
     rng = np.random.default_rng(2)
     x = O.rbf(rng.normal(0, 6, (96, 1536)).astype(np.float32), O.RNE)
     a = ref_kernels.run_rows(op, x, valid=valid)
