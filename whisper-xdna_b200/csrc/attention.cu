@@ -248,6 +248,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();   // Q, K and V come from the previous kernel
 
   if (warp == 0) {
     if (lane == 0) {
@@ -606,6 +608,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();   // Q, K and V come from the previous kernel
 
   if (warp == 0) {
     if (lane == 0) {
@@ -987,11 +991,12 @@ int attn_plan(AttnPlan* p, const void* q, const void* k, const void* v, void* o,
 
 int attn_run(const AttnPlan& p, cudaStream_t st) {
   if (p.persist) {
-    attention_persistent_kernel<<<p.grid, kAttThreads, kAttSmemPersist, st>>>(p.tmQ, p.tmK,
-                                                                               p.tmV, p.args);
+    WX_CUDA_TRY(launch_k(attention_persistent_kernel, dim3(p.grid), dim3(kAttThreads),
+                         kAttSmemPersist, st, p.tmQ, p.tmK, p.tmV, p.args));
   } else {
     dim3 grid(p.args.num_q_tiles, p.args.H, p.B);
-    attention_kernel<<<grid, kAttThreads, kAttSmem, st>>>(p.tmQ, p.tmK, p.tmV, p.args);
+    WX_CUDA_TRY(launch_k(attention_kernel, grid, dim3(kAttThreads), kAttSmem, st, p.tmQ, p.tmK,
+                         p.tmV, p.args));
   }
   return check_launch("attention");
 }

@@ -12,6 +12,7 @@
 namespace wx {
 
 static thread_local std::string g_last_error;
+thread_local bool g_pdl = false;
 
 int fail(int code, const char* fmt, ...) {
   char buf[1024];

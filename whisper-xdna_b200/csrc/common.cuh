@@ -186,6 +186,20 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// The encoder's forward launches its kernels as programmatic dependents of the
+// kernel before them (PdlScope in wxb200_internal.h), so that a kernel's launch
+// and prologue (barrier set-up, tensor-memory allocation, descriptor prefetch)
+// overlap the previous kernel's last wave. Every such kernel calls pdl_wait()
+// before its first access to global memory: it returns once the previous
+// kernel has completed and its writes are visible (at once for a kernel not
+// launched as a dependent). pdl_launch_dependents() lets the next kernel's
+// CTAs start launching once every CTA of this one has issued it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- timers
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;

@@ -395,6 +395,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nnb = a.num_n_blocks, nkb = a.num_k_blocks;
+  pdl_wait();   // the operands and the residual come from the previous kernel
 
   if (warp == 0) {
     if (lane == 0) {
@@ -405,6 +406,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t issued = 0, issued_phase = 0;  // per-slot bits
       for (int tile = blockIdx.x; ok && tile < a.num_tiles; tile += gridDim.x) {
         const int m0 = (tile / nnb) * kGemmBM, n0 = (tile % nnb) * BN;
+        // the next kernel may start launching once every CTA is on its last tile
+        if (tile + (int)gridDim.x >= a.num_tiles) pdl_launch_dependents();
         for (int kb = 0; kb < nkb; kb++) {
           if (!mbar_wait(&empty[stage], phase ^ 1, a.err)) { ok = false; break; }
           issued |= 1u << stage;
@@ -681,6 +684,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Cfg<EPI, I8>::T
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nnb = a.num_n_blocks, nkb = a.num_k_blocks;
+  pdl_wait();   // the operands and the residual come from the previous kernel
   bool ok = true;
 
   if (warp == 0) {
@@ -690,6 +694,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Cfg<EPI, I8>::T
       uint32_t phase = 0;
       for (int tile = pair; ok && tile < a.num_tiles; tile += npairs) {
         const int m0 = (tile / nnb) * 256, n0 = (tile % nnb) * BN;
+        // the next kernel may start launching once every CTA is on its last tile
+        if (tile + npairs >= a.num_tiles) pdl_launch_dependents();
         for (int kb = 0; kb < nkb; kb++) {
           if (!mbar_wait(&empty[stage], phase ^ 1, a.err)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kGemm2StageBytes);
@@ -1042,13 +1048,12 @@ static int prepare_t(int bn, bool pair) {
 template <int BN, int EPI, bool I8>
 static int launch_t(const GemmPlan& p, cudaStream_t st) {
   if (p.pair) {
-    gemm2_bf16_kernel<EPI, I8><<<p.grid, Gemm2Cfg<EPI, I8>::THREADS, Gemm2Cfg<EPI, I8>::SMEM,
-                                 st>>>(
-        p.tmA, p.tmB, p.tmC, p.tmR, p.args);
+    WX_CUDA_TRY(launch_k(gemm2_bf16_kernel<EPI, I8>, dim3(p.grid), dim3(Gemm2Cfg<EPI, I8>::THREADS),
+                         Gemm2Cfg<EPI, I8>::SMEM, st, p.tmA, p.tmB, p.tmC, p.tmR, p.args));
     return check_launch(I8 ? "gemm_i8_pair" : "gemm_bf16_pair");
   }
-  gemm_bf16_kernel<BN, EPI, I8><<<p.grid, kGemmThreads, GemmCfg<BN>::SMEM, st>>>(p.tmA, p.tmB,
-                                                                                 p.args);
+  WX_CUDA_TRY(launch_k(gemm_bf16_kernel<BN, EPI, I8>, dim3(p.grid), dim3(kGemmThreads),
+                       GemmCfg<BN>::SMEM, st, p.tmA, p.tmB, p.args));
   return check_launch(I8 ? "gemm_i8" : "gemm_bf16");
 }
 

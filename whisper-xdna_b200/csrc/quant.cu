@@ -116,6 +116,8 @@ __global__ void __launch_bounds__(32 * kQuantWarps)
     quantize_rows_kernel(const T* __restrict__ in, int64_t rows, int64_t cols, int64_t ld,
                          const float* __restrict__ rowmax, int64_t rowmax_stride,
                          int8_t* __restrict__ q, int64_t ld_q, float* __restrict__ scale) {
+  pdl_launch_dependents();
+  pdl_wait();   // the rows (and their maxima) come from the previous kernel
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kQuantWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -189,20 +191,21 @@ int launch_quantize_rows(const void* in, int in_dtype, int64_t rows, int64_t col
   const unsigned grid = (unsigned)((rows + kQuantWarps - 1) / kQuantWarps);
   if (in_dtype == WX_DTYPE_F32) {
     const float* x = static_cast<const float*>(in);
+    // (a failed launch is picked up by check_launch below)
     if (vec)
-      quantize_rows_kernel<float, true><<<grid, 32 * kQuantWarps, 0, st>>>(
-          x, rows, cols, ld, rowmax, rowmax_stride, q, ld_q, scale);
+      (void)launch_k(quantize_rows_kernel<float, true>, dim3(grid), dim3(32 * kQuantWarps), 0, st,
+                     x, rows, cols, ld, rowmax, rowmax_stride, q, ld_q, scale);
     else
-      quantize_rows_kernel<float, false><<<grid, 32 * kQuantWarps, 0, st>>>(
-          x, rows, cols, ld, rowmax, rowmax_stride, q, ld_q, scale);
+      (void)launch_k(quantize_rows_kernel<float, false>, dim3(grid), dim3(32 * kQuantWarps), 0,
+                     st, x, rows, cols, ld, rowmax, rowmax_stride, q, ld_q, scale);
   } else {
     const uint16_t* x = static_cast<const uint16_t*>(in);
     if (vec)
-      quantize_rows_kernel<uint16_t, true><<<grid, 32 * kQuantWarps, 0, st>>>(
-          x, rows, cols, ld, rowmax, rowmax_stride, q, ld_q, scale);
+      (void)launch_k(quantize_rows_kernel<uint16_t, true>, dim3(grid), dim3(32 * kQuantWarps), 0,
+                     st, x, rows, cols, ld, rowmax, rowmax_stride, q, ld_q, scale);
     else
-      quantize_rows_kernel<uint16_t, false><<<grid, 32 * kQuantWarps, 0, st>>>(
-          x, rows, cols, ld, rowmax, rowmax_stride, q, ld_q, scale);
+      (void)launch_k(quantize_rows_kernel<uint16_t, false>, dim3(grid), dim3(32 * kQuantWarps), 0,
+                     st, x, rows, cols, ld, rowmax, rowmax_stride, q, ld_q, scale);
   }
   return check_launch("quantize_rows");
 }

@@ -700,6 +700,8 @@ __global__ void __launch_bounds__(256) layernorm_fp32_kernel(
     const void* __restrict__ in, const float* __restrict__ gamma,
     const float* __restrict__ beta, void* __restrict__ out, int64_t rows, int w, int64_t ld_in,
     int64_t ld_out, float eps, void* const* __restrict__ out_ind) {
+  pdl_launch_dependents();
+  pdl_wait();   // the rows come from the previous kernel
   if (out_ind) out = *out_ind;
   constexpr int NR = NV > 0 ? NV : 1;
   const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
@@ -790,6 +792,8 @@ __global__ void __launch_bounds__(256) layernorm_quant_kernel(
     const float* __restrict__ in, const float* __restrict__ gamma, const float* __restrict__ beta,
     int8_t* __restrict__ q, int64_t ld_q, float* __restrict__ scale, int64_t rows, int w,
     int64_t ld_in, float eps) {
+  pdl_launch_dependents();
+  pdl_wait();   // the rows come from the previous kernel
   const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
   for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
        row += (int64_t)gridDim.x * warps) {
@@ -854,8 +858,10 @@ static void launch_ln_fp32(int grid, cudaStream_t st, const void* in, const floa
                            const float* beta, void* out, int64_t rows, int w, int64_t ld_in,
                            int64_t ld_out, float eps, void* const* out_ind) {
   const int nv = (w + 127) / 128;
-#define WX_LN_CASE(N) \
-  layernorm_fp32_kernel<IB, OB, N><<<grid, 256, 0, st>>>(in, gamma, beta, out, rows, w, ld_in, ld_out, eps, out_ind)
+// (a failed launch is picked up by the caller's check_launch)
+#define WX_LN_CASE(N)                                                                         \
+  (void)launch_k(layernorm_fp32_kernel<IB, OB, N>, dim3(grid), dim3(256), 0, st, in, gamma,  \
+                 beta, out, rows, w, ld_in, ld_out, eps, out_ind)
   if (nv <= 3) WX_LN_CASE(3);
   else if (nv <= 4) WX_LN_CASE(4);
   else if (nv <= 6) WX_LN_CASE(6);
@@ -1086,8 +1092,9 @@ int launch_layernorm_quant_rows(const float* in, const float* gamma, const float
   if (cols > 2048) return fail(WX_ERR_UNSUPPORTED, "layernorm_quant: rows wider than 2048");
   const int grid = grid_for(rows, 8, 8);
   const int nv = ((int)cols + 127) / 128, w = (int)cols;
-#define WX_LNQ_CASE(N) \
-  layernorm_quant_kernel<N><<<grid, 256, 0, st>>>(in, gamma, beta, q, ld_q, scale, rows, w, ld_in, eps)
+#define WX_LNQ_CASE(N)                                                                     \
+  (void)launch_k(layernorm_quant_kernel<N>, dim3(grid), dim3(256), 0, st, in, gamma, beta, \
+                 q, ld_q, scale, rows, w, ld_in, eps)
   if (nv <= 3) WX_LNQ_CASE(3);
   else if (nv <= 4) WX_LNQ_CASE(4);
   else if (nv <= 6) WX_LNQ_CASE(6);

@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/wxb200.h"
 
@@ -48,6 +49,38 @@ int encode_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
 int sm_count();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Programmatic dependent launch (PDL) for the encoder's forward pass: while a
+// PdlScope(true) is alive on the calling thread, launch_k gives each kernel the
+// programmatic-stream-serialization attribute, so it may launch while the
+// kernel before it on the stream finishes; the kernels launched this way call
+// pdl_wait() (common.cuh) before touching global memory. Outside a scope
+// launch_k is a plain launch.
+extern thread_local bool g_pdl;
+struct PdlScope {
+  bool prev;
+  explicit PdlScope(bool on) : prev(g_pdl) { g_pdl = on; }
+  ~PdlScope() { g_pdl = prev; }
+  PdlScope(const PdlScope&) = delete;
+  PdlScope& operator=(const PdlScope&) = delete;
+};
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (g_pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Makes `dev` the calling thread's current device for a scope and restores
 // the caller's device after: an engine's entry points run on the device the

@@ -122,8 +122,41 @@ def setup(kernel, batch, dev="cuda", ctx=T):
     raise ValueError(f"unknown kernel {kernel!r}")
 
 
-def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T):
+def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T, graph=False):
+    """graph=True captures the `iters` launches in one CUDA graph and times its
+    replay, so kernels shorter than the host's per-call cost (small batches)
+    are timed as they run inside the encoder's graph, not at the rate the
+    host can issue them."""
     fn, flop, byt = setup(kernel, batch, ctx=ctx)
+    if graph:
+        if flush:
+            raise ValueError("graph timing does not flush L2 between launches")
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            for _ in range(warmup):
+                fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream()
+        e0.record(cur)
+        g.replay()
+        e1.record(cur)
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / iters
+        res = {"kernel": kernel, "batch": batch, "s": t, "flop": flop, "bytes": byt,
+               "flush_l2": False, "graph": True}
+        if kernel == "attention":
+            res["ctx"] = ctx
+        if flop:
+            res["tflops"] = flop / t / 1e12
+        res["gbs"] = byt / t / 1e9
+        return res
     # 1 GiB: its fill (~160 us) outlasts the host-side cost of one launch
     junk = torch.empty(1024 * 1024 * 1024 // 4, device="cuda") if flush else None
     st = torch.cuda.current_stream()
@@ -171,10 +204,12 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--flush", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="time the launches captured in one CUDA graph")
     ap.add_argument("--ctx", type=int, default=T,
                     help="attention only: frames per clip (T <= 1344 runs the persistent kernel)")
     a = ap.parse_args()
-    res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush, ctx=a.ctx)
+    res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush, ctx=a.ctx, graph=a.graph)
     res["device_error"] = L.device_error()
     print(json.dumps(res))
 
