@@ -409,6 +409,11 @@ __global__ void __launch_bounds__(kSmRegThreads, 2) softmax_rows_reg_kernel(
   uint4* buf = reinterpret_cast<uint4*>(smem + kExpTabBytes) + (size_t)warp * (NV * 32);
   const uint16_t* buf16 = reinterpret_cast<const uint16_t*>(buf);
   const bool do_scale = scale != 1.0f;
+  // In RNE mode with a bf16 scale (1/8 for attention scores), R(x * scale) is
+  // one bf16x2 multiply: the fp32 product of two bf16 values is exact, and the
+  // bf16x2 instruction rounds that exact product once, to nearest even.
+  const bool scale_bf16x2 = R == RND_RNE && do_scale && rbf<RND_RNE>(scale) == scale;
+  const __nv_bfloat162 scale2 = __float2bfloat162_rn(scale);
   for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
        row += (int64_t)gridDim.x * warps) {
     const uint16_t* src_row = in + row * ld_in;
@@ -429,9 +434,13 @@ __global__ void __launch_bounds__(kSmRegThreads, 2) softmax_rows_reg_kernel(
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         uint32_t& v = x[4 * k + j];
-        if (do_scale)
+        if (scale_bf16x2) {
+          const __nv_bfloat162 t = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&v), scale2);
+          v = *reinterpret_cast<const uint32_t*>(&t);
+        } else if (do_scale) {
           v = pack_bf16x2<R>(__fmul_rn(__uint_as_float(v << 16), scale),
                              __fmul_rn(__uint_as_float(v & 0xFFFF0000u), scale));
+        }
         if (c0 < 0 || c0 + 8 > w) {
           const int c = c0 + 2 * j;
           if (c < 0 || c >= w) v = (v & 0xFFFF0000u) | 0xFF80u;
@@ -470,7 +479,7 @@ __global__ void __launch_bounds__(kSmRegThreads, 2) softmax_rows_reg_kernel(
     // 16 fp32 lanes, lane l summing e over columns l, l+16, ... (softmax_row4_body.inc:31-40)
     float acc = 0.0f;
     if (lane < 16) {
-#pragma unroll 8
+#pragma unroll 16
       for (int c = lane; c < w; c += 16) acc = __fadd_rn(acc, bits_f32(buf16[c + h]));
     }
     const float sum = __shfl_sync(0xffffffffu, lane16_tree(acc), 0);
@@ -502,16 +511,17 @@ __global__ void __launch_bounds__(kSmRegThreads, 2) softmax_rows_reg_kernel(
             e[j] = lo | (hi << 16);
           }
         }
+        // packed fp32 pairs: each product and sum rounded on its own, as above
         uint32_t o[4];
+        const float2 ihi2 = make_float2(ihi, ihi), ilo2 = make_float2(ilo, ilo);
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          const float elo = __uint_as_float(e[j] << 16);
-          const float ehi = __uint_as_float(e[j] & 0xFFFF0000u);
-          if (VAR == 1)
-            o[j] = pack_bf16x2<R>(__fmul_rn(elo, ihi), __fmul_rn(ehi, ihi));
-          else
-            o[j] = pack_bf16x2<R>(__fadd_rn(__fmul_rn(elo, ihi), __fmul_rn(elo, ilo)),
-                                  __fadd_rn(__fmul_rn(ehi, ihi), __fmul_rn(ehi, ilo)));
+          const float2 ev = make_float2(__uint_as_float(e[j] << 16),
+                                        __uint_as_float(e[j] & 0xFFFF0000u));
+          float2 p;
+          if (VAR == 1) p = __fmul2_rn(ev, ihi2);
+          else p = __fadd2_rn(__fmul2_rn(ev, ihi2), __fmul2_rn(ev, ilo2));
+          o[j] = pack_bf16x2<R>(p.x, p.y);
         }
         if (c0 >= 0 && c0 + 8 <= w) {
           dst[u] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -598,53 +608,98 @@ __global__ void __launch_bounds__(256) layernorm_aie_kernel(
   }
 }
 
-// The same arithmetic for rows of up to 256 * NV - 7 columns, read as 16-byte
-// chunks from the row start rounded down to 16 bytes (the
-// softmax_rows_reg_kernel layout) with all of a row's loads in flight
-// together, then kept in shared memory for the 16-lane sums and the
-// normalisation; gamma / beta are staged in shared memory once per CTA.
+// The same arithmetic for rows of up to 256 * NV - 7 columns, one warp per
+// row, arranged for latency (a 1500-row call has about ten rows per SM, so a
+// row's own critical path is the kernel's time):
+//  - the row is read as 16-byte chunks from its start rounded down to 16
+//    bytes (the softmax_rows_reg_kernel layout) into registers, with all of
+//    its loads in flight together and issued before gamma / beta are staged;
+//  - the reference's 16 lane sums (lane l adds columns l, l+16, ... in order,
+//    layer_norm_gb.cc:61-67) run from registers: each lane scatters its
+//    elements into a lane-transposed copy in shared memory, t[l][k] =
+//    x[l + 16k], whose row stride (8m + 4 elements) makes the 8-byte reads of
+//    the 16 summing lanes hit 32 distinct banks; columns past the row are
+//    zeros, which leave the sums' bits unchanged (a sum that starts at +0
+//    never becomes -0);
+//  - in RNE mode R(x - mean) and R(d * inv) are bf16x2 subtractions and
+//    products of bf16 operands: fp32 carries more than 2 * 8 + 2 significand
+//    bits, so the reference's fp32 operation followed by the bf16 rounding
+//    equals the single correctly rounded bf16x2 result; gamma / beta are
+//    applied in fp32, each product and sum rounded on its own.
 template <int R, int NV>
 __global__ void __launch_bounds__(256) layernorm_aie_reg_kernel(
     const uint16_t* __restrict__ in, const float* __restrict__ gamma,
     const float* __restrict__ beta, uint16_t* __restrict__ out, int64_t rows, int w,
-    int64_t ld_in, int64_t ld_out, float eps) {
+    int64_t ld_in, int64_t ld_out, float eps, int tstride) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const int warps = blockDim.x >> 5, warp = warp_id(), lane = lane_id();
+  const int warps = blockDim.x / 32, warp = warp_id(), lane = lane_id();
   const bool affine = gamma != nullptr || beta != nullptr;
-  float* g_s = reinterpret_cast<float*>(smem);             // [w] gamma, then [w] beta
-  float* b_s = g_s + w;
-  uint4* buf = reinterpret_cast<uint4*>(smem + (((size_t)2 * w * 4 + 15) & ~(size_t)15)) +
-               (size_t)warp * (NV * 32);
-  const uint16_t* buf16 = reinterpret_cast<const uint16_t*>(buf);
-  if (affine) {
-    for (int c = threadIdx.x; c < w; c += blockDim.x) {
-      g_s[c] = gamma ? gamma[c] : 1.0f;
-      b_s[c] = beta ? beta[c] : 0.0f;
-    }
-  }
-  __syncthreads();
-  const float inv_n = __fdiv_rn(1.0f, (float)w);                          // :69
-  for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
-       row += (int64_t)gridDim.x * warps) {
-    const uint16_t* src_row = in + row * ld_in;
-    const int h = chunk_head(src_row);
+  const int wp = (w + 3) & ~3;                                 // gamma / beta stride
+  float* g_s = reinterpret_cast<float*>(smem);                 // [wp] gamma, then [wp] beta
+  float* b_s = g_s + wp;
+  uint16_t* tbuf = reinterpret_cast<uint16_t*>(g_s + 2 * wp) + (size_t)warp * 16 * tstride;
+  const int kcols = (w + 15) >> 4;                             // columns of t per lane row
+  const int kread = (kcols + 3) & ~3;                          // read in groups of four
+  const float inv_n = __fdiv_rn(1.0f, (float)w);                       // :69
+  int64_t row = (int64_t)blockIdx.x * warps + warp;
+  uint32_t x[NV * 4];
+  int h = 0;
+  auto load_row = [&](int64_t r) {
+    const uint16_t* src_row = in + r * ld_in;
+    h = chunk_head(src_row);
     const int nch = (w + h + 7) >> 3;
     const uint4* src = reinterpret_cast<const uint4*>(src_row - h);
 #pragma unroll
     for (int k = 0; k < NV; k++) {
       uint4 q = make_uint4(0u, 0u, 0u, 0u);
       if (lane + 32 * k < nch) q = __ldg(src + lane + 32 * k);
-      buf[lane + 32 * k] = q;
+      x[4 * k] = q.x; x[4 * k + 1] = q.y; x[4 * k + 2] = q.z; x[4 * k + 3] = q.w;
+    }
+  };
+  if (row < rows) load_row(row);
+  if (affine) {
+    for (int c = threadIdx.x; c < wp; c += blockDim.x) {
+      g_s[c] = c < w ? (gamma ? gamma[c] : 1.0f) : 0.0f;
+      b_s[c] = c < w ? (beta ? beta[c] : 0.0f) : 0.0f;
+    }
+  }
+  __syncthreads();
+  for (; row < rows; row += (int64_t)gridDim.x * warps) {
+    if (row != (int64_t)blockIdx.x * warps + warp) load_row(row);
+    // t: zero the last read group of every lane row, then scatter the row
+    for (int i = lane; i < 16 * (kread - (kcols - 1 > 0 ? kcols - 1 : 0)); i += 32) {
+      const int l = i & 15, k = (kcols > 0 ? kcols - 1 : 0) + (i >> 4);
+      tbuf[l * tstride + k] = 0;
     }
     __syncwarp();
-    // pass 1 (:61-67): sum and sum of squares in 16 fp32 lanes
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int c0 = 8 * (lane + 32 * k) - h;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int c = c0 + j;
+        if (c >= 0 && c < w)
+          tbuf[(c & 15) * tstride + (c >> 4)] = (uint16_t)(x[4 * k + (j >> 1)] >> (16 * (j & 1)));
+      }
+    }
+    __syncwarp();
+    // pass 1 (:61-67): sum and sum of squares in 16 fp32 lanes, in column order
     float s1 = 0.0f, s2 = 0.0f;
     if (lane < 16) {
+      const uint2* tl = reinterpret_cast<const uint2*>(tbuf + lane * tstride);
 #pragma unroll 4
-      for (int c = lane; c < w; c += 16) {
-        const float x = bits_f32(buf16[c + h]);
-        s1 = __fadd_rn(s1, x);
-        s2 = __fadd_rn(s2, __fmul_rn(x, x));
+      for (int q = 0; q < kread / 4; q++) {
+        const uint2 v = tl[q];
+        const float e0 = __uint_as_float(v.x << 16), e1 = __uint_as_float(v.x & 0xFFFF0000u);
+        const float e2 = __uint_as_float(v.y << 16), e3 = __uint_as_float(v.y & 0xFFFF0000u);
+        s1 = __fadd_rn(s1, e0);
+        s2 = __fadd_rn(s2, __fmul_rn(e0, e0));
+        s1 = __fadd_rn(s1, e1);
+        s2 = __fadd_rn(s2, __fmul_rn(e1, e1));
+        s1 = __fadd_rn(s1, e2);
+        s2 = __fadd_rn(s2, __fmul_rn(e2, e2));
+        s1 = __fadd_rn(s1, e3);
+        s2 = __fadd_rn(s2, __fmul_rn(e3, e3));
       }
     }
     s1 = __shfl_sync(0xffffffffu, lane16_tree(s1), 0);
@@ -653,10 +708,34 @@ __global__ void __launch_bounds__(256) layernorm_aie_reg_kernel(
     const float var = __fsub_rn(__fmul_rn(s2, inv_n), __fmul_rn(mean, mean));  // :71
     const float inv = rsqrt_nr(__fadd_rn(var, eps));                     // :72
     const float mb = rbf<R>(mean), ib = rbf<R>(inv);                     // :74-77
-    auto norm = [&](float x, int c) -> float {                           // :80-85
-      float o = rbf<R>(__fmul_rn(rbf<R>(__fsub_rn(x, mb)), ib));
-      if (affine) o = rbf<R>(__fadd_rn(__fmul_rn(o, g_s[c]), b_s[c]));
-      return o;
+    const __nv_bfloat162 mb2 = __float2bfloat162_rn(mb), ib2 = __float2bfloat162_rn(ib);
+    // o = R(R(x - mean) * inv) of two bf16 values packed in a word (:80-85),
+    // then R(o * gamma + beta) for columns c, c + 1
+    auto norm2 = [&](uint32_t xw, int c, bool pair_in_row) -> uint32_t {
+      float o0, o1;
+      if (R == RND_RNE) {
+        const __nv_bfloat162 d = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&xw), mb2);
+        const __nv_bfloat162 o = __hmul2(d, ib2);
+        const uint32_t ow = *reinterpret_cast<const uint32_t*>(&o);
+        if (!affine) return ow;
+        o0 = __uint_as_float(ow << 16);
+        o1 = __uint_as_float(ow & 0xFFFF0000u);
+      } else {
+        o0 = rbf<R>(__fmul_rn(rbf<R>(__fsub_rn(__uint_as_float(xw << 16), mb)), ib));
+        o1 = rbf<R>(__fmul_rn(rbf<R>(__fsub_rn(__uint_as_float(xw & 0xFFFF0000u), mb)), ib));
+        if (!affine) return pack_bf16x2<R>(o0, o1);
+      }
+      float2 g, b;
+      if (pair_in_row) {
+        g = *reinterpret_cast<const float2*>(g_s + c);
+        b = *reinterpret_cast<const float2*>(b_s + c);
+      } else {
+        g = make_float2(c >= 0 && c < w ? g_s[c] : 0.0f, c + 1 >= 0 && c + 1 < w ? g_s[c + 1] : 0.0f);
+        b = make_float2(c >= 0 && c < w ? b_s[c] : 0.0f, c + 1 >= 0 && c + 1 < w ? b_s[c + 1] : 0.0f);
+      }
+      // scalar products and sums: gamma is a full fp32 value, so the product
+      // is inexact and must stay a separate rounding (never an fma)
+      return pack_bf16x2<R>(__fadd_rn(__fmul_rn(o0, g.x), b.x), __fadd_rn(__fmul_rn(o1, g.y), b.y));
     };
     uint16_t* dst_row = out + row * ld_out;
     const int ho = chunk_head(dst_row);
@@ -667,16 +746,24 @@ __global__ void __launch_bounds__(256) layernorm_aie_reg_kernel(
       const int u = lane + 32 * k;
       if (u < ncho) {
         const int c0 = 8 * u - ho;
+        uint32_t xs[4];
+        if (ho == h) {
+          xs[0] = x[4 * k]; xs[1] = x[4 * k + 1]; xs[2] = x[4 * k + 2]; xs[3] = x[4 * k + 3];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int c = c0 + 2 * j;
+            const uint32_t lo = (c >= 0 && c < w) ? tbuf[(c & 15) * tstride + (c >> 4)] : 0u;
+            const uint32_t hi =
+                (c + 1 >= 0 && c + 1 < w) ? tbuf[((c + 1) & 15) * tstride + ((c + 1) >> 4)] : 0u;
+            xs[j] = lo | (hi << 16);
+          }
+        }
+        const bool full = c0 >= 0 && c0 + 8 <= w;
         uint32_t o[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int c = c0 + 2 * j;
-          const bool in0 = c >= 0 && c < w, in1 = c + 1 >= 0 && c + 1 < w;
-          const float x0 = in0 ? bits_f32(buf16[c + h]) : 0.0f;
-          const float x1 = in1 ? bits_f32(buf16[c + 1 + h]) : 0.0f;
-          o[j] = pack_bf16x2<R>(norm(x0, in0 ? c : 0), norm(x1, in1 ? c + 1 : 0));
-        }
-        if (c0 >= 0 && c0 + 8 <= w) {
+        for (int j = 0; j < 4; j++) o[j] = norm2(xs[j], c0 + 2 * j, full && (c0 % 2 == 0));
+        if (full) {
           dst[u] = make_uint4(o[0], o[1], o[2], o[3]);
         } else {
 #pragma unroll
@@ -1017,7 +1104,11 @@ int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, cons
       const int w = (int)cols;
       const int chunks = (w + 14) / 8;
       const int nvc = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 192 ? 6 : 8;
-      const size_t smem = (((size_t)2 * w * 4 + 15) & ~(size_t)15) + (size_t)8 * nvc * 32 * 16;
+      // per warp a lane-transposed copy of its row: 16 lane rows of
+      // tstride = 8m + 4 >= ceil(w / 16) elements, padded to a multiple of 4
+      const int kcols = (w + 15) / 16;
+      const int tstride = ((kcols + 3) + 3) / 8 * 8 + 4;
+      const size_t smem = (size_t)2 * ((w + 3) & ~3) * 4 + (size_t)8 * 16 * tstride * 2;
       const int grid = grid_for(rows, 8, 8);
       const uint16_t* i16 = reinterpret_cast<const uint16_t*>(in);
       uint16_t* o16 = reinterpret_cast<uint16_t*>(out);
@@ -1025,7 +1116,7 @@ int launch_layernorm_rows(const void* in, int in_dtype, const float* gamma, cons
   do {                                                                                        \
     auto k = layernorm_aie_reg_kernel<R, N>;                                                  \
     WX_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
-    k<<<grid, 256, smem, st>>>(i16, gamma, beta, o16, rows, w, ld_in, ld_out, eps);           \
+    k<<<grid, 256, smem, st>>>(i16, gamma, beta, o16, rows, w, ld_in, ld_out, eps, tstride);  \
   } while (0)
 #define WX_LNR_NV(R)                           \
   do {                                         \

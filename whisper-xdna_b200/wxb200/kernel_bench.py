@@ -122,11 +122,16 @@ def setup(kernel, batch, dev="cuda", ctx=T):
     raise ValueError(f"unknown kernel {kernel!r}")
 
 
-def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T, graph=False):
+def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T, graph=False,
+                flush_mode="write"):
     """graph=True captures the `iters` launches in one CUDA graph and times its
     replay, so kernels shorter than the host's per-call cost (small batches)
     are timed as they run inside the encoder's graph, not at the rate the
     host can issue them."""
+    """flush_mode: how L2 is emptied between launches with flush=True: "write"
+    fills a 1 GiB buffer (L2 is left full of dirty lines, whose write-back the
+    timed kernel then pays for as it evicts them), "read" sums it (L2 is left
+    full of clean lines)."""
     fn, flop, byt = setup(kernel, batch, ctx=ctx)
     if graph:
         if flush:
@@ -158,7 +163,8 @@ def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T, graph=F
         res["gbs"] = byt / t / 1e9
         return res
     # 1 GiB: its fill (~160 us) outlasts the host-side cost of one launch
-    junk = torch.empty(1024 * 1024 * 1024 // 4, device="cuda") if flush else None
+    junk = torch.ones(1024 * 1024 * 1024 // 4, device="cuda") if flush else None
+    junk_sum = torch.empty((), device="cuda")
     st = torch.cuda.current_stream()
     for _ in range(warmup):
         fn()
@@ -170,7 +176,10 @@ def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T, graph=F
         # the event pair brackets the kernel, not the host's launch overhead.
         evs = []
         for _ in range(iters):
-            junk.fill_(1.0)
+            if flush_mode == "read":
+                torch.sum(junk, dim=0, out=junk_sum)
+            else:
+                junk.fill_(1.0)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
             fn()
@@ -189,6 +198,8 @@ def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T, graph=F
     t = total / iters
     res = {"kernel": kernel, "batch": batch, "s": t, "flop": flop, "bytes": byt,
            "flush_l2": bool(flush)}
+    if flush:
+        res["flush_mode"] = flush_mode
     if kernel == "attention":
         res["ctx"] = ctx
     if flop:
@@ -204,12 +215,14 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--flush", action="store_true")
+    ap.add_argument("--flush-mode", choices=["write", "read"], default="write")
     ap.add_argument("--graph", action="store_true",
                     help="time the launches captured in one CUDA graph")
     ap.add_argument("--ctx", type=int, default=T,
                     help="attention only: frames per clip (T <= 1344 runs the persistent kernel)")
     a = ap.parse_args()
-    res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush, ctx=a.ctx, graph=a.graph)
+    res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush, ctx=a.ctx, graph=a.graph,
+                      flush_mode=a.flush_mode)
     res["device_error"] = L.device_error()
     print(json.dumps(res))
 
