@@ -37,9 +37,12 @@ METRIC = "large-v3 encoder clips/s @ctx1500"
 UNIT = "clips/s"
 N_MELS, D, N_HEAD, N_LAYER, FFN, CTX = 128, 1280, 20, 32, 5120, 1500
 # DRAM bytes (read + write) of one attention launch per clip, measured by ncu
-# on a 4-clip launch (profiles/attention_ncu_b4.md: 46.14 MB read, 0.28 MB
-# written); Q, K and V are read once, O stays in L2 at that size.
-ATTN_DRAM_BYTES_PER_CLIP = (46.173e6 + 0.453e6) / 4
+# on one launch at the benchmarked 64 clips (profiles/attention_ncu_b64.md:
+# 738.08 MB read = Q, K, V once; 227.49 MB written of the 245.8 MB of O)
+ATTN_DRAM_BYTES_PER_CLIP = (738.076e6 + 227.493e6) / 64
+# nominal fp32 FMA rate (148 SMs x 128 lanes x 2 FLOP x 1.965 GHz) for the
+# log-mel kernel's DFT, which runs on the FMA pipe (no measured fp32 peak)
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 # ctx 512: 32 layers at T = 512 + the conv frontend over 1024 frames
 FLOP_PER_CLIP_512 = (32 * (8 * 512 * 1280 * 1280 + 4 * 512 * 1280 * 5120 + 4 * 512 * 512 * 1280)
                      + 2 * 1024 * 384 * 1280 + 2 * 512 * 3840 * 1280)
@@ -213,33 +216,8 @@ class Clocks:
 def make_weights_fast(seed):
     """Random N(0, 0.02) large-v3 weights (torch CPU generator, bf16-exact),
     LayerNorm 1 / 0, sinusoidal positions, in the reference's W-dict layout."""
-    import numpy as np
-    import torch
-
-    def sinusoids(length, channels, max_timescale=10000):
-        inc = np.log(max_timescale) / (channels // 2 - 1)
-        t = np.arange(length)[:, None] * np.exp(-inc * np.arange(channels // 2))[None, :]
-        return np.concatenate([np.sin(t), np.cos(t)], axis=1).astype(np.float32)
-
-    g = torch.Generator().manual_seed(seed)
-    rn = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
-    W = {"w.conv1.weight": rn(D, N_MELS, 3), "w.conv1.bias": rn(D),
-         "w.conv2.weight": rn(D, D, 3), "w.conv2.bias": rn(D),
-         "w.positional_embedding": sinusoids(CTX, D),
-         "w.ln_post.weight": np.ones(D, np.float32), "w.ln_post.bias": np.zeros(D, np.float32)}
-    for l in range(N_LAYER):
-        p = f"w.blocks.{l}."
-        W[p + "attn_ln.weight"] = np.ones(D, np.float32)
-        W[p + "attn_ln.bias"] = np.zeros(D, np.float32)
-        W[p + "mlp_ln.weight"] = np.ones(D, np.float32)
-        W[p + "mlp_ln.bias"] = np.zeros(D, np.float32)
-        for n, s in (("attn.query.weight", (D, D)), ("attn.query.bias", (D,)),
-                     ("attn.key.weight", (D, D)), ("attn.value.weight", (D, D)),
-                     ("attn.value.bias", (D,)), ("attn.out.weight", (D, D)),
-                     ("attn.out.bias", (D,)), ("mlp.0.weight", (FFN, D)), ("mlp.0.bias", (FFN,)),
-                     ("mlp.2.weight", (D, FFN)), ("mlp.2.bias", (D,))):
-            W[p + n] = rn(*s)
-    return W
+    from wxb200.encoder import synthetic_weights
+    return synthetic_weights(N_MELS, D, FFN, N_LAYER, CTX, seed=seed)
 
 
 def kernel_rooflines(batch, peaks):
@@ -261,6 +239,11 @@ def kernel_rooflines(batch, peaks):
         r = time_kernel(k, iters=20, flush=True)
         r["frac_of_measured_hbm"] = r["gbs"] / peaks["hbm_gbs"]
         rows[k] = r
+    # the device log-mel frontend (row f2): this rank's clips of 30 s audio
+    r = time_kernel("log_mel", batch=batch, iters=5)
+    r["clips_per_s"] = batch / r["s"]
+    r["frac_of_nominal_fp32"] = r["tflops"] / FP32_NOMINAL_TFLOPS
+    res["log_mel"] = r
     return res, rows
 
 
@@ -440,8 +423,8 @@ def run_b200(args, rank, world, local_rank):
                 "frac": k["tflops"] / peaks["bf16_tflops"], "peak_source": peaks["src"],
                 "flop_per_launch": 4.0 * B * CTX * CTX * D,
                 "traffic": ATTN_DRAM_BYTES_PER_CLIP * B,
-                "traffic_note": "dram read+write per launch, from the ncu capture in "
-                                "profiles/attention_ncu_b4.md scaled by clips (4 -> B)",
+                "traffic_note": "dram read+write per launch, from one ncu capture at 64 clips "
+                                "(profiles/attention_ncu_b64.md), per clip x B",
                 "whole_step": {"achieved": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12,
                                "frac": FLOP_PER_CLIP * B / (t_dev / args.steps) / 1e12
                                / peaks["bf16_tflops"]}}

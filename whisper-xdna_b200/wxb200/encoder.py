@@ -39,6 +39,34 @@ def geometry(W, n_layer=None, n_head=None):
     return n_mels, d, nh, nl, ffn, n_ctx
 
 
+def synthetic_weights(n_mels=128, d=1280, ffn=5120, n_layer=32, n_ctx=1500, seed=1):
+    """Random N(0, 0.02) weights of a Whisper encoder in the reference's W-dict
+    layout (bf16-exact fp32 arrays, torch CPU generator), LayerNorm gamma 1 and
+    beta 0, sinusoidal positions: the synthetic stand-in for a checkpoint that
+    the benchmarks use (defaults: large-v3 geometry)."""
+    g = torch.Generator().manual_seed(seed)
+    rn = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    inc = np.log(10000) / (d // 2 - 1)
+    t = np.arange(n_ctx)[:, None] * np.exp(-inc * np.arange(d // 2))[None, :]
+    pos = np.concatenate([np.sin(t), np.cos(t)], axis=1).astype(np.float32)
+    W = {"w.conv1.weight": rn(d, n_mels, 3), "w.conv1.bias": rn(d),
+         "w.conv2.weight": rn(d, d, 3), "w.conv2.bias": rn(d),
+         "w.positional_embedding": pos,
+         "w.ln_post.weight": np.ones(d, np.float32), "w.ln_post.bias": np.zeros(d, np.float32)}
+    for l in range(n_layer):
+        p = f"w.blocks.{l}."
+        for ln in ("attn_ln", "mlp_ln"):
+            W[p + ln + ".weight"] = np.ones(d, np.float32)
+            W[p + ln + ".bias"] = np.zeros(d, np.float32)
+        for n, sh in (("attn.query.weight", (d, d)), ("attn.query.bias", (d,)),
+                      ("attn.key.weight", (d, d)), ("attn.value.weight", (d, d)),
+                      ("attn.value.bias", (d,)), ("attn.out.weight", (d, d)),
+                      ("attn.out.bias", (d,)), ("mlp.0.weight", (ffn, d)), ("mlp.0.bias", (ffn,)),
+                      ("mlp.2.weight", (d, ffn)), ("mlp.2.bias", (d,))):
+            W[p + n] = rn(*sh)
+    return W
+
+
 class Encoder:
     """A Whisper encoder resident on one GPU.
 

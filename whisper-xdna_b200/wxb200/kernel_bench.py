@@ -2,7 +2,7 @@
 
     PYTHONPATH=whisper-xdna_b200 python -m wxb200.kernel_bench --kernel attention --batch 4
 
-Kernels: attention, fc1 (GEMM + GELU), fc2 (GEMM + residual), qkv, outproj,
+Kernels: encoder (a whole forward), attention, fc1 (GEMM + GELU), fc2 (GEMM + residual), qkv, outproj,
 their int8 twins fc1_i8, fc2_i8, qkv_i8, outproj_i8 (the int8 mode's GEMMs),
 quantize_bf16 (fc2's input rows, maxima given) and quantize_f32 (an LN output),
 layernorm (fp32 -> bf16, the encoder's), and the standalone row ops at the
@@ -25,10 +25,20 @@ from . import ops
 D, H, FFN, T = 1280, 20, 5120, 1500
 
 
-def setup(kernel, batch, dev="cuda", ctx=T):
+def setup(kernel, batch, dev="cuda", ctx=T, layers=32):
     """Return (fn, flop_per_launch, bytes_per_launch) for one kernel; ctx is
-    the frame count of the attention kernel's clips (the encoder's T)."""
+    the frame count of the attention kernel's clips (the encoder's T).
+    kernel "encoder": one whole large-v3 forward of `batch` clips (ctx 1500,
+    `layers` layers, random weights), the captured launch sequence."""
     g = torch.Generator(device=dev).manual_seed(0)
+    if kernel == "encoder":
+        from .encoder import Encoder, synthetic_weights
+        enc = Encoder(synthetic_weights(n_layer=layers), n_layer=layers, max_batch=batch)
+        mel = torch.rand(batch, 128, 2 * T, device=dev, generator=g) * 2 - 0.8
+        out = torch.empty(batch, T, D, device=dev)
+        flop = batch * (layers * (8 * T * D * D + 4 * T * D * FFN + 4 * T * T * D)
+                        + 2 * (2 * T) * (3 * 128) * D + 2 * T * (3 * D) * D)
+        return (lambda: enc.forward(mel, out=out)), float(flop), batch * (128 * 2 * T + T * D) * 4
     M = batch * T
     rn = lambda *s, sc=1.0: (torch.randn(*s, device=dev, generator=g) * sc)
     if kernel == "attention":
@@ -123,7 +133,7 @@ def setup(kernel, batch, dev="cuda", ctx=T):
 
 
 def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T, graph=False,
-                flush_mode="write"):
+                flush_mode="write", layers=32):
     """graph=True captures the `iters` launches in one CUDA graph and times its
     replay, so kernels shorter than the host's per-call cost (small batches)
     are timed as they run inside the encoder's graph, not at the rate the
@@ -132,7 +142,7 @@ def time_kernel(kernel, batch=4, iters=10, warmup=3, flush=False, ctx=T, graph=F
     fills a 1 GiB buffer (L2 is left full of dirty lines, whose write-back the
     timed kernel then pays for as it evicts them), "read" sums it (L2 is left
     full of clean lines)."""
-    fn, flop, byt = setup(kernel, batch, ctx=ctx)
+    fn, flop, byt = setup(kernel, batch, ctx=ctx, layers=layers)
     if graph:
         if flush:
             raise ValueError("graph timing does not flush L2 between launches")
@@ -216,13 +226,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--flush", action="store_true")
     ap.add_argument("--flush-mode", choices=["write", "read"], default="write")
+    ap.add_argument("--layers", type=int, default=32, help="encoder only: layers")
     ap.add_argument("--graph", action="store_true",
                     help="time the launches captured in one CUDA graph")
     ap.add_argument("--ctx", type=int, default=T,
                     help="attention only: frames per clip (T <= 1344 runs the persistent kernel)")
     a = ap.parse_args()
     res = time_kernel(a.kernel, a.batch, a.iters, a.warmup, a.flush, ctx=a.ctx, graph=a.graph,
-                      flush_mode=a.flush_mode)
+                      flush_mode=a.flush_mode, layers=a.layers)
     res["device_error"] = L.device_error()
     print(json.dumps(res))
 
