@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "ln_row.cuh"
 
 namespace wx {
 
@@ -175,11 +176,6 @@ __global__ void __launch_bounds__(128) gelu_poly4_kernel(const void* __restrict_
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 // The 16 lane partial sums of lanes 0..15 reduced by the halving tree
@@ -805,55 +801,39 @@ __global__ void __launch_bounds__(256) layernorm_fp32_kernel(
   for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
        row += (int64_t)gridDim.x * warps) {
     float4 v[NR];
-    float s = 0.0f;
+    float mean, rstd;
     if (NV > 0) {
 #pragma unroll
       for (int i = 0; i < NR; i++) {
         const int c = (i * 32 + lane) * 4;
         v[i] = c < w ? load4(row, c) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-#pragma unroll
-      for (int i = 0; i < NR; i++) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+      ln_row_stats<NR>(v, w, lane, eps, mean, rstd);
     } else {
+      // wider than the register buckets: the same sums over the row re-read from L2
+      float s = 0.0f;
       for (int c = lane * 4; c < w; c += 128) {
         const float4 t = load4(row, c);
         s += (t.x + t.y) + (t.z + t.w);
       }
-    }
-    const float mean = warp_sum(s) / (float)w;
-    float q = 0.0f;
-    if (NV > 0) {
-#pragma unroll
-      for (int i = 0; i < NR; i++) {
-        const int c = (i * 32 + lane) * 4;
-        if (c < w) {
-          const float a = v[i].x - mean, b = v[i].y - mean, d = v[i].z - mean, e = v[i].w - mean;
-          q += (a * a + b * b) + (d * d + e * e);
-        }
-      }
-    } else {
+      mean = warp_sum(s) / (float)w;
+      float q = 0.0f;
       for (int c = lane * 4; c < w; c += 128) {
         const float4 t = load4(row, c);
         const float a = t.x - mean, b = t.y - mean, d = t.z - mean, e = t.w - mean;
         q += (a * a + b * b) + (d * d + e * e);
       }
+      rstd = 1.0f / sqrtf(warp_sum(q) / (float)w + eps);
     }
-    const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)w + eps);
     auto emit = [&](int c, float4 t) {
-      const float4 g = gamma ? __ldg(reinterpret_cast<const float4*>(gamma + c))
-                             : make_float4(1.f, 1.f, 1.f, 1.f);
-      const float4 b = beta ? __ldg(reinterpret_cast<const float4*>(beta + c))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float y0 = (t.x - mean) * rstd * g.x + b.x, y1 = (t.y - mean) * rstd * g.y + b.y;
-      const float y2 = (t.z - mean) * rstd * g.z + b.z, y3 = (t.w - mean) * rstd * g.w + b.w;
+      const float4 y = ln_affine4(t, mean, rstd, gamma, beta, c);
       if (OUT_BF16) {
         uint2 o;
-        o.x = pack_bf16x2_rne(y0, y1);
-        o.y = pack_bf16x2_rne(y2, y3);
+        o.x = pack_bf16x2_rne(y.x, y.y);
+        o.y = pack_bf16x2_rne(y.z, y.w);
         *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + row * ld_out + c) = o;
       } else {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + row * ld_out + c) =
-            make_float4(y0, y1, y2, y3);
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + row * ld_out + c) = y;
       }
     };
     if (NV > 0) {
@@ -885,38 +865,20 @@ __global__ void __launch_bounds__(256) layernorm_quant_kernel(
   for (int64_t row = (int64_t)blockIdx.x * warps + warp; row < rows;
        row += (int64_t)gridDim.x * warps) {
     float4 v[NV];
-    float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < NV; i++) {
       const int c = (i * 32 + lane) * 4;
       v[i] = c < w ? __ldg(reinterpret_cast<const float4*>(in + row * ld_in + c))
                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-#pragma unroll
-    for (int i = 0; i < NV; i++) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    const float mean = warp_sum(s) / (float)w;
-    float qs = 0.0f;
-#pragma unroll
-    for (int i = 0; i < NV; i++) {
-      const int c = (i * 32 + lane) * 4;
-      if (c < w) {
-        const float a = v[i].x - mean, b = v[i].y - mean, d = v[i].z - mean, e = v[i].w - mean;
-        qs += (a * a + b * b) + (d * d + e * e);
-      }
-    }
-    const float rstd = 1.0f / sqrtf(warp_sum(qs) / (float)w + eps);
+    float mean, rstd;
+    ln_row_stats<NV>(v, w, lane, eps, mean, rstd);
     uint32_t mx = 0;
 #pragma unroll
     for (int i = 0; i < NV; i++) {
       const int c = (i * 32 + lane) * 4;
       if (c < w) {
-        const float4 g = gamma ? __ldg(reinterpret_cast<const float4*>(gamma + c))
-                               : make_float4(1.f, 1.f, 1.f, 1.f);
-        const float4 b = beta ? __ldg(reinterpret_cast<const float4*>(beta + c))
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 t = v[i];
-        v[i] = make_float4((t.x - mean) * rstd * g.x + b.x, (t.y - mean) * rstd * g.y + b.y,
-                           (t.z - mean) * rstd * g.z + b.z, (t.w - mean) * rstd * g.w + b.w);
+        v[i] = ln_affine4(v[i], mean, rstd, gamma, beta, c);
         mx = max(mx, max(max(__float_as_uint(v[i].x) & 0x7FFFFFFFu,
                              __float_as_uint(v[i].y) & 0x7FFFFFFFu),
                          max(__float_as_uint(v[i].z) & 0x7FFFFFFFu,
@@ -944,18 +906,20 @@ template <bool IB, bool OB>
 static void launch_ln_fp32(int grid, cudaStream_t st, const void* in, const float* gamma,
                            const float* beta, void* out, int64_t rows, int w, int64_t ld_in,
                            int64_t ld_out, float eps, void* const* out_ind) {
-  const int nv = (w + 127) / 128;
+  const int nv = w > 16 * 128 ? 0 : ln_nv_bucket(w);
 // (a failed launch is picked up by the caller's check_launch)
 #define WX_LN_CASE(N)                                                                         \
   (void)launch_k(layernorm_fp32_kernel<IB, OB, N>, dim3(grid), dim3(256), 0, st, in, gamma,  \
                  beta, out, rows, w, ld_in, ld_out, eps, out_ind)
-  if (nv <= 3) WX_LN_CASE(3);
-  else if (nv <= 4) WX_LN_CASE(4);
-  else if (nv <= 6) WX_LN_CASE(6);
-  else if (nv <= 8) WX_LN_CASE(8);
-  else if (nv <= 10) WX_LN_CASE(10);
-  else if (nv <= 16) WX_LN_CASE(16);
-  else WX_LN_CASE(0);
+  switch (nv) {
+    case 3: WX_LN_CASE(3); break;
+    case 4: WX_LN_CASE(4); break;
+    case 6: WX_LN_CASE(6); break;
+    case 8: WX_LN_CASE(8); break;
+    case 10: WX_LN_CASE(10); break;
+    case 16: WX_LN_CASE(16); break;
+    default: WX_LN_CASE(0);
+  }
 #undef WX_LN_CASE
 }
 
@@ -1182,16 +1146,18 @@ int launch_layernorm_quant_rows(const float* in, const float* gamma, const float
                 "in, gamma and beta 16-byte aligned, q 4-byte aligned");
   if (cols > 2048) return fail(WX_ERR_UNSUPPORTED, "layernorm_quant: rows wider than 2048");
   const int grid = grid_for(rows, 8, 8);
-  const int nv = ((int)cols + 127) / 128, w = (int)cols;
+  const int w = (int)cols;
 #define WX_LNQ_CASE(N)                                                                     \
   (void)launch_k(layernorm_quant_kernel<N>, dim3(grid), dim3(256), 0, st, in, gamma, beta, \
                  q, ld_q, scale, rows, w, ld_in, eps)
-  if (nv <= 3) WX_LNQ_CASE(3);
-  else if (nv <= 4) WX_LNQ_CASE(4);
-  else if (nv <= 6) WX_LNQ_CASE(6);
-  else if (nv <= 8) WX_LNQ_CASE(8);
-  else if (nv <= 10) WX_LNQ_CASE(10);
-  else WX_LNQ_CASE(16);
+  switch (ln_nv_bucket(w)) {
+    case 3: WX_LNQ_CASE(3); break;
+    case 4: WX_LNQ_CASE(4); break;
+    case 6: WX_LNQ_CASE(6); break;
+    case 8: WX_LNQ_CASE(8); break;
+    case 10: WX_LNQ_CASE(10); break;
+    default: WX_LNQ_CASE(16);
+  }
 #undef WX_LNQ_CASE
   return check_launch("layernorm_quant");
 }
