@@ -170,6 +170,13 @@ int wx_gemm_i8(const int8_t* A, const int8_t* B, const float* sa, const float* s
                const float* bias, const float* R, void* C, int64_t M, int64_t N, int64_t K,
                int64_t lda, int64_t ldb, int64_t ldc, int64_t ldr, int epilogue, float* rowmax,
                void* stream);
+/* The unquantised control of the same probe, q_matmul_factory("fp32")
+ * (bench/probe_int8_decode.py:58-60, numpy float32 A @ B + bias): C = A @ B^T
+ * (+ bias[n]) in fp32 on the FMA pipe, A (M x K) and B (N x K) fp32 row-major
+ * with row strides lda, ldb, ldc (elements), bias NULL or N floats. Each
+ * output is one fp32 FMA chain over k in ascending order. */
+int wx_gemm_f32(const float* A, const float* B, const float* bias, float* C, int64_t M,
+                int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream);
 
 /* ------------------------------------------------------------ attention */
 

@@ -172,6 +172,32 @@ def test_q_matmul_equals_reference(cuda, mode):
         assert out.dtype == np.float32 and np.array_equal(out, z[f"s{i}_{mode}"]), (i, mode)
 
 
+@pytest.mark.parametrize("M,K,N", [(1, 1, 1), (5, 7, 3), (130, 300, 257), (1500, 1280, 384),
+                                   (300, 5120, 130)])
+def test_gemm_f32_against_float64(cuda, M, K, N):
+    """wx_gemm_f32 (the fp32 control's kernel): ragged tiles and K steps, bias,
+    against the float64 product. The bound is fp32 round-off of a K-term FMA
+    chain, K * 2^-24 relative to sum |a b|."""
+    rng = np.random.default_rng(M * 7 + N)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = rng.standard_normal((N, K)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    got = ops.gemm_f32(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(),
+                       bias=torch.from_numpy(b).cuda()).cpu().numpy()
+    ref = A.astype(np.float64) @ W.astype(np.float64).T + b
+    mag = np.abs(A).astype(np.float64) @ np.abs(W).astype(np.float64).T + np.abs(b)
+    assert np.all(np.abs(got - ref) <= (K + 2) * 2.0 ** -24 * mag + 1e-30)
+    # strided views: a column window of A and of the output
+    Ab = torch.zeros(M, K + 9, device="cuda")
+    Ab[:, 4:4 + K] = torch.from_numpy(A).cuda()
+    ob = torch.full((M, N + 5), 7.0, device="cuda")
+    ops.gemm_f32(Ab[:, 4:4 + K], torch.from_numpy(W).cuda(), out=ob[:, 2:2 + N])
+    o = ob.cpu().numpy()
+    assert np.all(o[:, :2] == 7.0) and np.all(o[:, 2 + N:] == 7.0)
+    assert np.all(np.abs(o[:, 2:2 + N] - (ref - b)) <= (K + 2) * 2.0 ** -24 * mag + 1e-30)
+    assert L.device_error() == 0
+
+
 def test_q_matmul_fp32_control(cuda):
     z = np.load(GOLD / "quant_gemm.npz")
     A, B, bias = gemm_inputs(*[int(v) for v in z["shapes"][0]], seed=100)

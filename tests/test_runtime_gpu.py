@@ -145,3 +145,18 @@ def test_fault_injection_surfaces_as_exception(rt, monkeypatch):
     with pytest.raises(RuntimeError, match="injected"):
         rt.attn_chain(q, q, q, 6, 0.35)
     assert rt.fallbacks == []
+
+
+def test_encoder_engine_rebuilt_when_an_array_is_replaced(rt):
+    """The engine cache follows the arrays of W: replacing one (here ln_post's
+    bias, +1 on every output) builds a new engine; an unchanged W reuses it."""
+    W = R.make_weights("tiny", seed=5, n_layer=1, n_ctx=64)
+    mel = R.make_mel(80, 128, seed=5)
+    from wxb200.encoder import encoder
+    a = encoder(W, mel, rt.matmul, n_layer=1, n_head=6)
+    eng = rt.encoder_engine(W, 1, 6)
+    assert rt.encoder_engine(W, 1, 6) is eng
+    W["w.ln_post.bias"] = np.asarray(W["w.ln_post.bias"], np.float32) + 1.0
+    b = encoder(W, mel, rt.matmul, n_layer=1, n_head=6)
+    assert rt.encoder_engine(W, 1, 6) is not eng
+    assert np.allclose(b, a + 1.0, atol=1e-5)

@@ -17,6 +17,8 @@
 // half-to-even (__float2int_rn), so each quantised value equals numpy's. The
 // kernels are HBM-bound: a bf16 row is read once (twice when the row maximum is
 // computed here, the second time from L2) and written as int8.
+//
+// The same probe's unquantised control ("fp32") is the fp32 GEMM at the end.
 #include <cstdint>
 
 #include "common.cuh"
@@ -210,6 +212,100 @@ int launch_quantize_rows(const void* in, int in_dtype, int64_t rows, int64_t col
   return check_launch("quantize_rows");
 }
 
+// ---------------------------------------------------------------- fp32 GEMM
+// The unquantised control of q_matmul_factory ("fp32": A @ B + bias in numpy
+// float32, bench/probe_int8_decode.py:58-60): C = A @ B^T (+ bias) on the FMA
+// pipe. 128 x 128 tiles, 256 threads, each an 8 x 8 block of outputs (rows
+// 4 ty + {0..3} and 64 + 4 ty + {0..3}, columns likewise from tx) so that its
+// operands come from shared memory as float4; K in steps of 16, the next step
+// loaded into registers while the current one is multiplied. Every output is
+// one fp32 FMA chain over k in ascending order.
+constexpr int kF32Tile = 128, kF32Step = 16;
+
+__global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A,
+                                                       const float* __restrict__ B,
+                                                       const float* __restrict__ bias,
+                                                       float* __restrict__ C, int M, int N, int K,
+                                                       int64_t lda, int64_t ldb, int64_t ldc) {
+  __shared__ __align__(16) float sA[2][kF32Step][kF32Tile];
+  __shared__ __align__(16) float sB[2][kF32Step][kF32Tile];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * kF32Tile, n0 = blockIdx.x * kF32Tile;
+  // staging: element e = tid + 256 i of a 128 x 16 tile is row e / 16, k e % 16
+  float ra[8], rb[8];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int e = tid + 256 * i, r = e >> 4, k = k0 + (e & 15);
+      ra[i] = (m0 + r < M && k < K) ? A[(int64_t)(m0 + r) * lda + k] : 0.0f;
+      rb[i] = (n0 + r < N && k < K) ? B[(int64_t)(n0 + r) * ldb + k] : 0.0f;
+    }
+  };
+  auto stash = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int e = tid + 256 * i;
+      sA[buf][e & 15][e >> 4] = ra[i];
+      sB[buf][e & 15][e >> 4] = rb[i];
+    }
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+  const int steps = (K + kF32Step - 1) / kF32Step;
+  fetch(0);
+  stash(0);
+  __syncthreads();
+  for (int s = 0; s < steps; s++) {
+    const int buf = s & 1;
+    if (s + 1 < steps) fetch((s + 1) * kF32Step);
+#pragma unroll
+    for (int k = 0; k < kF32Step; k++) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&sA[buf][k][4 * ty]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&sA[buf][k][64 + 4 * ty]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&sB[buf][k][4 * tx]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&sB[buf][k][64 + 4 * tx]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+    }
+    if (s + 1 < steps) {
+      stash(buf ^ 1);   // the other buffer was last read before the previous barrier
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int m = m0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + i - 4);
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int n = n0 + (j < 4 ? 4 * tx + j : 64 + 4 * tx + j - 4);
+      if (n < N) C[(int64_t)m * ldc + n] = bias ? __fadd_rn(acc[i][j], bias[n]) : acc[i][j];
+    }
+  }
+}
+
+int launch_gemm_f32(const float* A, const float* B, const float* bias, float* C, int64_t M,
+                    int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t st) {
+  if (M < 0 || N < 0 || K < 0) return fail(WX_ERR_INVALID, "gemm_f32: negative shape");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(WX_ERR_UNSUPPORTED, "gemm_f32: dimension exceeds 2^31");
+  if (M == 0 || N == 0) return WX_OK;
+  if (!A || !B || !C) return fail(WX_ERR_INVALID, "gemm_f32: NULL operand");
+  if (lda < K || ldb < K || ldc < N) return fail(WX_ERR_INVALID, "gemm_f32: leading dimension too small");
+  const int64_t gx = (N + kF32Tile - 1) / kF32Tile, gy = (M + kF32Tile - 1) / kF32Tile;
+  if (gy > 65535) return fail(WX_ERR_UNSUPPORTED, "gemm_f32: M above %d", 65535 * kF32Tile);
+  (void)launch_k(gemm_f32_kernel, dim3((unsigned)gx, (unsigned)gy), dim3(256), 0, st, A, B, bias,
+                 C, (int)M, (int)N, (int)K, lda, ldb, ldc);
+  return check_launch("gemm_f32");
+}
+
 }  // namespace wx
 
 extern "C" {
@@ -237,6 +333,11 @@ int wx_gemm_i8(const int8_t* A, const int8_t* B, const float* sa, const float* s
   WX_TRY(wx::gemm_plan_i8(&p, A, B, sa, sw, bias, R, C, M, N, K, lda, ldb, ldc, ldr, epilogue,
                           rowmax));
   return wx::gemm_run(p, wx::as_stream(stream));
+}
+
+int wx_gemm_f32(const float* A, const float* B, const float* bias, float* C, int64_t M,
+                int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  return wx::launch_gemm_f32(A, B, bias, C, M, N, K, lda, ldb, ldc, wx::as_stream(stream));
 }
 
 }  // extern "C"

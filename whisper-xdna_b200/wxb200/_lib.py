@@ -52,6 +52,7 @@ SIGNATURES = {
     "wx_quantize_rows": (_i, [_p, _i, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _p]),
     "wx_gemm_i8": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i,
                         _p, _p]),
+    "wx_gemm_f32": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p]),
     "wx_attention": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f, _p]),
     "wx_mlp_bf16_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),
     "wx_encoder_create": (_i, [_c.POINTER(_p), _i, _i, _i, _i, _i, _i, _i, _i]),

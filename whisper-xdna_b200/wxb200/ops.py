@@ -117,6 +117,24 @@ def gemm(A, W, bias=None, residual=None, out=None, epilogue=None):
     return out
 
 
+def gemm_f32(A, W, bias=None, out=None):
+    """A @ W^T (+ bias) in fp32 on the FMA pipe: A (M, K), W (N, K) float32
+    CUDA tensors with unit column stride; each output sums k in ascending order."""
+    _mat(A, "A", (torch.float32,))
+    _mat(W, "W", (torch.float32,))
+    M, K = A.shape
+    N, K2 = W.shape
+    if K != K2:
+        raise ValueError(f"inner dimensions differ: {K} vs {K2}")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32, device=A.device)
+    _mat(out, "out", (torch.float32,))
+    b = _vec(bias, N, "bias")
+    L.check(L.lib().wx_gemm_f32(_ptr(A), _ptr(W), _ptr(b), _ptr(out), M, N, K, A.stride(0),
+                                W.stride(0), out.stride(0), _stream()))
+    return out
+
+
 def _outvec(t, n, name):
     """A float32 CUDA vector written in place: must be contiguous already."""
     _vec(t, n, name)

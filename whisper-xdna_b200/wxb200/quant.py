@@ -8,7 +8,7 @@ E.np_matmul, n_layer, n_head, fold_bias=False) as the probe calls it
 (:140-142). Modes:
   "perchan"   per-token activation scales, per-column weight scales
   "pertensor" per-token activation scales, one weight scale per matrix
-  "fp32"      the unquantised control, A @ B in fp32 (TF32 off)
+  "fp32"      the unquantised control, A @ B in fp32 (wx_gemm_f32, FMA pipe)
 The quantisation (wx_quantize_rows), the int8 product with s32 accumulation
 and the (r * sa) * sw scaling (wx_gemm_i8) reproduce the reference's float32
 arithmetic step for step, so the result equals the probe's numpy output bit
@@ -44,17 +44,9 @@ def q_matmul_factory(mode):
         dev = torch.device("cuda", torch.cuda.current_device())
         dA = torch.from_numpy(A).to(dev)
         b = None if bias is None else torch.from_numpy(np.ascontiguousarray(bias, np.float32)).to(dev)
-        if mode == "fp32":
-            prev = torch.backends.cuda.matmul.allow_tf32
-            torch.backends.cuda.matmul.allow_tf32 = False
-            try:
-                r = dA @ torch.from_numpy(B).to(dev)
-            finally:
-                torch.backends.cuda.matmul.allow_tf32 = prev
-            if b is not None:
-                r = r + b
-            return r.cpu().numpy()
         dW = torch.from_numpy(np.ascontiguousarray(B.T)).to(dev)   # (N, K)
+        if mode == "fp32":
+            return ops.gemm_f32(dA, dW, bias=b).cpu().numpy()
         qa, sa = ops.quantize_rows(dA)
         qw, sw = quantize_weight(dW, mode)
         out = ops.gemm_i8(qa, qw, sa, sw, bias=b)

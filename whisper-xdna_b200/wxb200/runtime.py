@@ -82,7 +82,7 @@ class B200RT:
         self._keep = []       # the registered arrays, so their ids stay unique
         self._wdev = {}       # (key, tag) -> device tensor
         self._akey = None     # (akey, tensor): the last named activation
-        self._engines = {}    # (id(W), n_layer, n_head, gelu) -> Encoder
+        self._engines = {}    # (id(W), n_layer, n_head, gelu) -> (array ids, arrays, Encoder)
         # the reference's state containers, read/cleared by the STT server
         # (serve/npu_stt_server.py:315-325, 379-387)
         self._chains, self._scratch, self._scratch_owner = {}, {}, {}
@@ -276,14 +276,23 @@ class B200RT:
 
     # ---------------------------------------------------------------- encoder
     def encoder_engine(self, W, n_layer=None, n_head=None, max_batch=1, gelu=None):
-        """The device-resident encoder for weight dict W, built once per W."""
+        """The device-resident encoder for weight dict W, built once per W and
+        rebuilt when an array of W has been replaced by another object. Arrays
+        are taken as immutable, as register_weights takes them (src/rawxrt.py:
+        307-316): one changed in place keeps its engine."""
         gelu = gelu or self.gelu_mode
         key = (id(W), n_layer, n_head, gelu)
-        eng = self._engines.get(key)
+        arrays = [(k, v) for k, v in sorted(W.items()) if k.startswith("w.")]
+        ids = tuple((k, id(v)) for k, v in arrays)
+        hit = self._engines.get(key)
+        eng = hit[2] if hit is not None and hit[0] == ids else None
         if eng is None or eng.max_batch < max_batch:
+            if hit is not None:
+                hit[2].close()
             eng = Encoder(W, n_layer=n_layer, n_head=n_head, max_batch=max_batch, gelu=gelu,
                           device=self.device.index)
-            self._engines[key] = eng
+            # the arrays are held so that their ids cannot be reused by new ones
+            self._engines[key] = (ids, [v for _, v in arrays], eng)
             self._keep.append(W)
         return eng
 
