@@ -412,6 +412,10 @@ def run_b200(args, rank, world, local_rank):
     value = total_clips / t_dev
     e2e = total_clips / t_e2e
     peaks = load_peaks()
+    if lat is not None:
+        # the whole one-clip forward against the dense bf16 peak
+        lat["tflops"] = FLOP_PER_CLIP / (lat["device_ms"] * 1e-3) / 1e12
+        lat["frac_of_bf16_peak"] = lat["tflops"] / peaks["bf16_tflops"]
     roof, cpu = None, None
     kernels, row_ops = {}, {}
     if rank == 0:
