@@ -103,6 +103,19 @@ def setup(kernel, batch, dev="cuda", ctx=T, layers=32):
         fn = lambda: ops.layer_norm_rows(x, gm, bt, out=h, mode=L.WX_LN_FP32)
         return fn, 0.0, M * D * (4 + 2) + 2 * D * 4
     # standalone row ops, BASELINE sizes (batch ignored)
+    if kernel.startswith("copy:"):
+        # the floor for moving the same bytes: torch's device copy (y <- x) of
+        # the named row op's input and output tensors, for scale
+        name = kernel[5:]
+        if name not in ("gelu", "gelu_f32", "softmax", "layernorm_gb"):
+            raise ValueError(f"copy: of {name!r}")
+        shape = {"gelu": (1500, 5120), "gelu_f32": (1500, 5120), "softmax": (20 * 1500, 1500),
+                 "layernorm_gb": (1500, 1280)}[name]
+        x = rn(*shape)
+        if name != "gelu_f32":
+            x = x.to(torch.bfloat16)
+        y = torch.empty(*shape, device=dev, dtype=torch.bfloat16)
+        return (lambda: y.copy_(x)), 0.0, x.numel() * x.element_size() + y.numel() * 2
     if kernel == "gelu":
         x = (rn(1500, 5120) * 3).to(torch.bfloat16)
         y = torch.empty_like(x)
