@@ -105,6 +105,21 @@ def test_gemm_residual_in_place(cuda, M, N, K):
     assert err < 1e-5, err
 
 
+@pytest.mark.parametrize("M,N,K", [(19200, 1280, 5120), (19017, 1280, 4096)])
+def test_gemm_residual_in_place_equals_separate_output(cuda, M, N, K):
+    """Long-K residual GEMMs on CTA pairs (fc2's shape) add the residual in
+    place by a TMA reduce-add in L2 when C is the residual; the bits equal those
+    of the path that loads the residual into the epilogue (a separate output)."""
+    A, W = rand_bf16((M, K), 11), rand_bf16((N, K), 12, 0.02)
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(13)).cuda() * 0.1
+    x = torch.randn(M, N, generator=torch.Generator().manual_seed(14)).cuda()
+    y = torch.empty_like(x)
+    ops.gemm(A, W, bias=bias, residual=x, out=y, epilogue=L.WX_EPI_F32_RESID)
+    ops.gemm(A, W, bias=bias, residual=x, out=x, epilogue=L.WX_EPI_F32_RESID)
+    assert torch.equal(x, y)
+    assert L.device_error() == 0
+
+
 @pytest.mark.parametrize("M,N,K", [(1500, 5120, 1280), (1500, 1536, 384), (77, 264, 72)])
 def test_gemm_gelu_epilogue_matches_g4f(cuda, M, N, K):
     """fc1 -> g4f fused: bit-exact to the oracle's g4f of the fp32 accumulator."""
