@@ -287,8 +287,7 @@ class B200RT:
         hit = self._engines.get(key)
         eng = hit[2] if hit is not None and hit[0] == ids else None
         if eng is None or eng.max_batch < max_batch:
-            if hit is not None:
-                hit[2].close()
+            # a replaced engine is freed by Encoder.__del__ once no caller holds it
             eng = Encoder(W, n_layer=n_layer, n_head=n_head, max_batch=max_batch, gelu=gelu,
                           device=self.device.index)
             # the arrays are held so that their ids cannot be reused by new ones
