@@ -9,6 +9,9 @@ its own one-clip forward, through the device entry point and through the
 pipelined host entry point (submit_host / wait_host). Clips 0 and 63 are also
 checked against the torch fp32 CPU encoder.
 
+The int8 mode is checked the same way at 64 clips (its CTA-pair int8 GEMMs
+against the one-SM kernels of a one-clip forward).
+
 The reference's own gate does the same at its production configuration:
 cosine against torch, then equality to a golden output
 (tests/test_encoder_golden.py:99-116 of the reference).
@@ -114,3 +117,21 @@ def test_large_v3_32_layers_batch64(cuda):
     print(f"MEASURED large-v3 32 layers clip 0: cos {cos:.8f}, rel L2 {R.rel_l2(got0, ref):.3e}")
     assert cos >= COS_32L, cos
     assert L.device_error() == 0
+
+
+def test_int8_batch64_every_clip_equals_its_single_clip_forward(cuda):
+    """The int8 mode at the same shape (bench.py --quant int8-perchan): CTA-pair
+    int8 GEMMs with the 16-warp GELU epilogue, the fc1 row maxima folded by
+    atomics and the residual added in place, against the one-SM kernels of a
+    one-clip forward; every clip bit for bit."""
+    W = R.make_weights("large-v3", seed=1, n_layer=2)
+    enc = Encoder(W, n_layer=2, n_head=20, max_batch=B, quant="int8-perchan")
+    try:
+        mel_dev = torch.from_numpy(clip_mels(3000, first_seed=3000)).cuda()
+        out = enc.forward(mel_dev)
+        torch.cuda.synchronize()
+        assert bool(torch.isfinite(out).all())
+        check_batch_equals_single(enc, mel_dev, out)
+        assert L.device_error() == 0
+    finally:
+        enc.close()
