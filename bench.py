@@ -235,7 +235,7 @@ def kernel_rooflines(batch, peaks):
             r["frac_of_measured_hbm"] = r["gbs"] / peaks["hbm_gbs"]
         res[k] = r
     rows = {}
-    for k in ("gelu", "gelu_f32", "softmax", "layernorm_gb"):
+    for k in ("gelu", "gelu_1536", "gelu_f32", "softmax", "layernorm_gb", "layernorm_gb_384"):
         r = time_kernel(k, iters=20, flush=True)
         r["frac_of_measured_hbm"] = r["gbs"] / peaks["hbm_gbs"]
         rows[k] = r

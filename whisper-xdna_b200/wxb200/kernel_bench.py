@@ -107,15 +107,28 @@ def setup(kernel, batch, dev="cuda", ctx=T, layers=32):
         # the floor for moving the same bytes: torch's device copy (y <- x) of
         # the named row op's input and output tensors, for scale
         name = kernel[5:]
-        if name not in ("gelu", "gelu_f32", "softmax", "layernorm_gb"):
+        shapes = {"gelu": (1500, 5120), "gelu_1536": (1500, 1536), "gelu_f32": (1500, 5120),
+                  "softmax": (20 * 1500, 1500), "layernorm_gb": (1500, 1280),
+                  "layernorm_gb_384": (1500, 384)}
+        if name not in shapes:
             raise ValueError(f"copy: of {name!r}")
-        shape = {"gelu": (1500, 5120), "gelu_f32": (1500, 5120), "softmax": (20 * 1500, 1500),
-                 "layernorm_gb": (1500, 1280)}[name]
+        shape = shapes[name]
         x = rn(*shape)
         if name != "gelu_f32":
             x = x.to(torch.bfloat16)
         y = torch.empty(*shape, device=dev, dtype=torch.bfloat16)
         return (lambda: y.copy_(x)), 0.0, x.numel() * x.element_size() + y.numel() * 2
+    if kernel == "gelu_1536":   # the sweep's smaller GELU (whisper-tiny's FFN width)
+        x = (rn(1500, 1536) * 3).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        return (lambda: ops.gelu_poly4(x, out=y, rounding=L.WX_ROUND_RNE)), 0.0, x.numel() * 4
+    if kernel == "layernorm_gb_384":   # the sweep's smaller LayerNorm (whisper-tiny's width)
+        x = (rn(1500, 384) * 3).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        gm, bt = rn(384, sc=0.1) + 1, rn(384, sc=0.1)
+        fn = lambda: ops.layer_norm_rows(x, gm, bt, out=y, mode=L.WX_LN_AIE,
+                                         rounding=L.WX_ROUND_RNE)
+        return fn, 0.0, x.numel() * 4 + 2 * 384 * 4
     if kernel == "gelu":
         x = (rn(1500, 5120) * 3).to(torch.bfloat16)
         y = torch.empty_like(x)
