@@ -121,12 +121,26 @@ constexpr int kOCol = 4 * kSBufCols;              // O_A at 384, O_B at 448
 // P of half 0 (keys 0-47) at column 0 of its S buffer, of half 1 at column 64
 __host__ __device__ constexpr int p_col(int half) { return half ? 64 : 0; }
 constexpr float kRescaleThreshold = 8.0f;         // log2 units
+// Tile B's issuer starts its first S this many SM cycles after tile A's. The
+// two tiles' softmax warps share each sub-partition's SFU; started together
+// they run their exponentials (SFU-bound) and their max / load phases (SFU
+// idle) in step. Measured at 64 clips x 20 heads x 1500 frames: 1128 us
+// without an offset, 1091-1095 us at 700-1,000 cycles, 1107 us at 400,
+// 1140-1154 us at 1,300-1,600.
+constexpr long long kTileBOffsetCycles = 800;
 static_assert(kOCol + 2 * kAttHD <= kAttTmemCols, "tensor memory budget");
 static_assert((1 + 4 * kAttStages + 4 + 4 + 4 + 2) * 8 + 4 <= kAttBarBytes, "barrier area");
 static_assert((2 + 2 + 4 * kAttStages + 4 + 4 + 4 + 2) * 8 + 4 <= kAttBarBytes,
               "barrier area (persistent)");
 static_assert(kAttSmemPersist <= 227 * 1024, "shared memory per CTA");
 static_assert(2 * kQBytes % 1024 == 0 && kKVBytes % 1024 == 0, "SW128 tiles 1024-aligned");
+
+// a busy wait of n SM cycles (one thread; the clock only moves forward)
+__device__ __forceinline__ void spin_cycles(long long n) {
+  const long long t0 = clock64();
+  while (clock64() - t0 < n) {
+  }
+}
 
 template <int N>
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
@@ -367,6 +381,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           if (j + 2 < nkv) return issue_s(j + 2, std::integral_constant<int, (m + 2) % 6>());
           return true;
         };
+        if (t == 1) spin_cycles(kTileBOffsetCycles);
         if (ok) ok = issue_s(0, std::integral_constant<int, 0>());
         if (ok && nkv > 1) ok = issue_s(1, std::integral_constant<int, 1>());
         for (int j = 0; ok && j < nkv; j += 6) {
@@ -759,6 +774,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           if (g + 2 < G) return issue_s(g + 2, std::integral_constant<int, (m + 2) % 6>());
           return true;
         };
+        if (t == 1) spin_cycles(kTileBOffsetCycles);
         ok = issue_s(0, std::integral_constant<int, 0>());
         if (ok && G > 1) ok = issue_s(1, std::integral_constant<int, 1>());
         for (int g = 0; ok && g < G; g += 6) {
