@@ -38,8 +38,8 @@ UNIT = "clips/s"
 N_MELS, D, N_HEAD, N_LAYER, FFN, CTX = 128, 1280, 20, 32, 5120, 1500
 # DRAM bytes (read + write) of one attention launch per clip, measured by ncu
 # on one launch at the benchmarked 64 clips (profiles/attention_ncu_b64.md:
-# 738.08 MB read = Q, K, V once; 227.49 MB written of the 245.8 MB of O)
-ATTN_DRAM_BYTES_PER_CLIP = (738.076e6 + 227.493e6) / 64
+# 737.57 MB read = Q, K, V once; 226.14 MB written of the 245.8 MB of O)
+ATTN_DRAM_BYTES_PER_CLIP = (737.565e6 + 226.136e6) / 64
 # nominal fp32 FMA rate (148 SMs x 128 lanes x 2 FLOP x 1.965 GHz) for the
 # log-mel kernel's DFT, which runs on the FMA pipe (no measured fp32 peak)
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
