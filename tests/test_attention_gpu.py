@@ -50,7 +50,7 @@ def check(got, ref, v, tag="", l2_bar=5e-3, max_bar=1.5e-3):
 
 @pytest.mark.parametrize("B,T,H", [(1, 1500, 6), (1, 1500, 20), (2, 1500, 6), (16, 1500, 6),
                                    (1, 128, 2), (1, 100, 3), (3, 257, 4), (1, 1, 1),
-                                   (2, 512, 20)])
+                                   (2, 512, 20), (1, 3001, 2), (2, 1537, 3)])
 def test_attention_matches_fp32(cuda, B, T, H):
     qkv = qkv_rand(B, T, H, B * 1000 + T + H)
     d = H * 64
