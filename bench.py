@@ -388,25 +388,30 @@ def run_b200(args, rank, world, local_rank):
     # published 3344 ms per large-v3 pass is this batch-1 latency)
     lat = None
     if rank == 0:
+        # 30 untimed forwards first: right after the 64-clip loop the SM clock
+        # is still at the power cap's level, and a server encoding one window
+        # after another runs at its steady state
         one_d, one_o = mel[:1], out[:1]
-        for _ in range(3):
+        for _ in range(30):
             enc.forward(one_d, out=one_o)
         torch.cuda.synchronize()
         l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         l0.record(st)
-        for _ in range(20):
+        for _ in range(100):
             enc.forward(one_d, out=one_o)
         l1.record(st)
         torch.cuda.synchronize()
         one_h, one_oh = mel_np[:1], out_np[:1]
-        enc.forward_host(one_h, out=one_oh)
-        w1 = time.perf_counter()
-        for _ in range(10):
+        for _ in range(5):
             enc.forward_host(one_h, out=one_oh)
-        lat = {"device_ms": l0.elapsed_time(l1) / 20,
-               "e2e_ms": (time.perf_counter() - w1) / 10 * 1e3,
-               "note": "one clip per forward, ctx 1500; the reference publishes 3344 ms "
-                       "for this on its NPU"}
+        w1 = time.perf_counter()
+        for _ in range(20):
+            enc.forward_host(one_h, out=one_oh)
+        lat = {"device_ms": l0.elapsed_time(l1) / 100,
+               "e2e_ms": (time.perf_counter() - w1) / 20 * 1e3,
+               "note": "one clip per forward, ctx 1500, after 30 untimed forwards; device: "
+                       "100 forwards back to back; e2e: 20 synchronous host calls; the "
+                       "reference publishes 3344 ms for this on its NPU"}
 
     total_clips = B * world * args.steps
     value = total_clips / t_dev
